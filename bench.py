@@ -1,0 +1,428 @@
+#!/usr/bin/env python3
+"""Benchmark of the GQA decode hot path (Llama-3-8B shape).
+
+``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``
+
+One step = one decode over the HBM-resident cache of one batch: B=64
+sequences x 32 query heads over 8 KV heads, head_dim 128, 4096 cached tokens,
+bf16 ~ N(0,1)*0.5 (seed 1).  Under torchrun each rank runs its own batch of
+64 sequences (weak scaling: global batch = 64 x N; batch sharding has no
+data-path collective).  The metric is the KV-stream bandwidth, GB/s =
+sum(len) x Hkv x D x 2 (K and V) x 2 bytes / step time, summed over ranks,
+with queries/s = sequences / step time beside it.
+
+* ``value``: device time of K timed steps (CUDA events on the launching
+  stream, barrier + synchronize on both sides, max over ranks); inputs are
+  resident (1 GiB per step, larger than L2, so no flush is needed).
+* ``e2e``: the same metric through the public API with host buffers:
+  ``AttentionAccelerator.run_query`` with pinned host q/o (H2D of q, decode,
+  D2H of o, synchronous), wall-clock over K steps.
+* ``roofline``: the decode kernel's algorithmic bytes per launch / its mean
+  launch time, against the measured HBM copy bandwidth.
+* ``cpu_baseline``: the CPU oracle (restatement of the reference's
+  ``cpu_attention_numpy``) on the same workload, on this host's cores.
+* ``--impl reference``: times that CPU path (the reference implementation of
+  the path is CPU code) on rank 0 and prints its own line.
+"""
+
+from __future__ import annotations
+
+import os
+
+# The CPU baseline parallelises over (sequence, kv-head) pairs with one
+# thread per core, so the BLAS inside each NumPy call runs single-threaded;
+# like the reference harness (sw/board_performance.py:13-17) this is set
+# before NumPy is imported.
+for _name in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS", "NUMEXPR_NUM_THREADS"):
+    os.environ.setdefault(_name, "1")
+
+import argparse
+import json
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GQA decode KV-stream GB/s (% of HBM peak) & queries/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+PROFILE_SUMMARY = ROOT / "profiles" / "decode_llama3_8b_cfg2.txt"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per rank (default: config 2's 64)")
+    ap.add_argument("--seq-len", type=int, default=None)
+    ap.add_argument("--splits", type=int, default=0, help="force the split count (0 = planner)")
+    ap.add_argument("--chunk", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch from the committed ncu summary, if present."""
+    if not PROFILE_SUMMARY.exists():
+        return None
+    for line in PROFILE_SUMMARY.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling every 200 ms during the timed region."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_uuid: str | None):
+        self.path = Path(tempfile.mkstemp(prefix="lara_clocks_", suffix=".csv")[1])
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if gpu_uuid:
+            cmd += ["-i", gpu_uuid]
+        self.proc = None
+        try:
+            self.fh = self.path.open("w")
+            self.proc = subprocess.Popen(cmd, stdout=self.fh, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < 5.0 and self.path.stat().st_size == 0:
+            time.sleep(0.05)
+        self.t_start = self.t_end = None
+
+    def start(self):
+        self.t_start = time.time()
+
+    def stop(self):
+        self.t_end = time.time()
+        time.sleep(0.25)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.proc is not None and self.path.exists():
+            for line in self.path.read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                try:
+                    ts = time.mktime(time.strptime(parts[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                    rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10], parts[5]))
+                except ValueError:
+                    continue
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        lo, hi = (self.t_start or 0) - 1.0, (self.t_end or 1e18) + 1.0
+        inside = [r for r in rows if lo <= r[0] <= hi] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in inside),
+                "reasons": reasons, "samples": len(inside)}
+
+
+class CpuOracle:
+    """The CPU oracle's decode over (sequence, kv-head) pairs on a thread pool."""
+
+    def __init__(self, q, k, v, lens, threads: int):
+        import concurrent.futures as cf
+
+        import oracle
+
+        self.q, self.k, self.v, self.lens = q, k, v, lens
+        self.threads = max(1, threads)
+        self.pool = cf.ThreadPoolExecutor(max_workers=self.threads)
+        self._decode = oracle.decode_attention
+
+    def step(self, pairs) -> None:
+        chunks = [pairs[i::self.threads] for i in range(min(self.threads, len(pairs)))]
+        list(self.pool.map(lambda ps: self._decode(self.q, self.k, self.v, self.lens, pairs=ps), chunks))
+
+    def close(self) -> None:
+        self.pool.shutdown()
+
+
+def cpu_decode_rate(q, k, v, lens, seconds: float, threads: int):
+    """Time the CPU oracle on whole decode steps until ``seconds`` have passed.
+
+    Returns (GB/s, steps, elapsed)."""
+    B, Hkv = k.shape[0], k.shape[1]
+    pairs = [(b, h) for b in range(B) for h in range(Hkv)]
+    nbytes = int(np.sum(lens, dtype=np.int64)) * Hkv * k.shape[3] * 4
+    runner = CpuOracle(q, k, v, lens, threads)
+    done, t0 = 0, time.perf_counter()
+    try:
+        while True:
+            runner.step(pairs)
+            done += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+    finally:
+        runner.close()
+    return nbytes * done / el / 1e9, done, el
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+
+def run_reference(args, rank: int, world: int) -> int:
+    """CPU reference path (oracle port of cpu_attention_numpy), rank 0 only.
+
+    Each of the K timed steps decodes a bounded sample of the workload's
+    (sequence, kv-head) pairs, sized by a calibration so the K steps take
+    about a minute; the value is the sample's KV bytes over its time."""
+    if rank != 0:
+        return 0
+    import concurrent.futures as cf
+
+    import oracle
+    from lara_b200.workloads import CONFIGS
+
+    cfg = CONFIGS[2]
+    B = args.batch or cfg.batch
+    L = args.seq_len or cfg.seq_len
+    Hkv, D = cfg.n_kv_heads, cfg.head_dim
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    pack = oracle.fp32_to_bf16_u16
+    rng = np.random.default_rng(cfg.seed)
+    nb = min(B, max(1, -(-cores // Hkv)) * 2)  # sequences held on the host for the samples
+    q = pack(rng.standard_normal((nb, cfg.n_q_heads, D), dtype=np.float32) * np.float32(cfg.std))
+    k = pack(rng.standard_normal((nb, Hkv, L, D), dtype=np.float32) * np.float32(cfg.std))
+    v = pack(rng.standard_normal((nb, Hkv, L, D), dtype=np.float32) * np.float32(cfg.std))
+    lens = np.full(nb, L, np.int32)
+    all_pairs = [(b, h) for b in range(nb) for h in range(Hkv)]
+    runner = CpuOracle(q, k, v, lens, cores)
+    calib = all_pairs[:min(len(all_pairs), cores)]
+    runner.step(calib)
+    t0 = time.perf_counter()
+    runner.step(calib)
+    t_batch = time.perf_counter() - t0  # wall time of `cores` pairs in parallel
+    budget = min(2.0, 60.0 / max(args.steps, 1))
+    n_pairs = int(max(1, min(len(all_pairs), budget / max(t_batch, 1e-6) * len(calib))))
+    sample = all_pairs[:n_pairs]
+    for _ in range(min(args.warmup, 3)):
+        runner.step(sample)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        runner.step(sample)
+    t = (time.perf_counter() - t0) / max(args.steps, 1)
+    runner.close()
+    nbytes = n_pairs * L * D * 2 * 2
+    value = nbytes / t / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "global_batch": B * world, "seq_len": L, "n_q_heads": cfg.n_q_heads,
+                   "n_kv_heads": Hkv, "head_dim": D},
+        "queries_per_s": round(n_pairs / Hkv / t, 2),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{n_pairs} (sequence, kv-head) pairs x {L} tokens per step (of {B * Hkv}); the "
+                                   f"reference's implementation of this path is CPU NumPy "
+                                   f"(sw/board_performance.py:158-192), run as the oracle port on {cores} threads"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from lara_b200 import ops
+    from lara_b200.workloads import CONFIGS, make_decode_inputs
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[2]
+    B = args.batch or cfg.batch
+    L = args.seq_len or cfg.seq_len
+    q, k, v, lens = make_decode_inputs(cfg, dev, batch=B, seq_len=L, seed=cfg.seed + 1000 * rank)
+    lens_np = lens.cpu().numpy()
+    nbytes = cfg.kv_bytes(lens_np)
+    dec = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, L, dev, lens=lens_np,
+                      num_splits=args.splits, chunk_tokens=args.chunk)
+    o = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        dec(q, k, v, lens, out=o)
+    torch.cuda.synchronize(dev)
+    if ops.workspace_status(dec.workspace) != 0:
+        raise RuntimeError("decode kernel reported a device error status during warm-up")
+
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        uuid = None
+    sampler = ClockSampler(uuid)
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.start()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        dec(q, k, v, lens, out=o)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    sampler.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    clocks = sampler.summary()
+    if ops.workspace_status(dec.workspace) != 0:
+        raise RuntimeError("decode kernel reported a device error status")
+
+    # e2e through the public API with pinned host buffers
+    e2e_ms = None
+    h2d = d2h = 0
+    if not args.no_e2e:
+        import ctypes
+
+        from lara_b200 import _native
+        from lara_b200.attn_driver import AttentionAccelerator
+
+        with AttentionAccelerator(device=local_rank) as acc:
+            acc.configure_heads(cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, max_seq_len=L, batch=B)
+            # device-resident cache load through the C ABI (on_device = 1)
+            _native.check(_native.lib.lara_kv_load(acc._ctx, k.data_ptr(), v.data_ptr(),
+                                                   lens_np.ctypes.data_as(ctypes.c_void_p), L, 1), "kv_load")
+            q_host = q.view(torch.int16).cpu().pin_memory()
+            o_host = torch.empty_like(q_host).pin_memory()
+            qn = q_host.numpy().view(np.uint16)
+            on = o_host.numpy().view(np.uint16)
+            for _ in range(max(3, min(args.warmup, 20))):
+                acc.run_query(qn, out=on)
+            e2e_steps = max(10, args.steps // 4)
+            barrier()
+            t0 = time.perf_counter()
+            for _ in range(e2e_steps):
+                acc.run_query(qn, out=on)
+            e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+            barrier()
+            h2d, d2h = qn.nbytes, on.nbytes
+            # the API result equals the stateless kernel's
+            if not np.array_equal(on, o.view(torch.int16).cpu().numpy().view(np.uint16)):
+                raise RuntimeError("run_query output differs from the kernel output")
+
+    # max over ranks
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms or 0.0], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), (float(t[1]) if e2e_ms is not None else None)
+
+    if rank != 0:
+        return 0
+    peak, peak_kind = measured_peak()
+    value = nbytes * world / (ms * 1e-3) / 1e9
+    achieved = nbytes / (ms * 1e-3) / 1e9  # one launch per step on each GPU
+    traffic = profiled_traffic()
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        qn_, kn_, vn_ = (t.view(torch.int16).cpu().numpy().view(np.uint16) for t in (q, k, v))
+        cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+        gbs, steps_done, el = cpu_decode_rate(qn_, kn_, vn_, lens_np, args.cpu_seconds, cores)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"{steps_done} full decode step(s) of this workload ({B} seqs x {L} tokens) in "
+                         f"{el:.1f} s, oracle restatement of sw/board_performance.py:158-192, {cores} threads"}
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "global_batch": B * world, "batch_per_gpu": B, "seq_len": L,
+                   "n_q_heads": cfg.n_q_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
+                   "parallelism": f"batch-sharded x{world}", "l2": "inputs (1 GiB/GPU) larger than L2, no flush",
+                   "splits": dec.plan.num_splits, "chunk_tokens": dec.plan.chunk_tokens},
+        "queries_per_s": round(B * world / (ms * 1e-3), 1),
+        "pct_hbm_peak": round(100.0 * achieved / peak, 2),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s", "algorithmic_bytes_per_launch": nbytes},
+        "cpu_baseline": cpu,
+        "e2e": None if e2e_ms is None else {
+            "value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
+            "api": "AttentionAccelerator.run_query (pinned host q/o)"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world != 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,241 @@
+/*
+ * lara_b200.h -- C ABI of liblara_b200.so, the B200 (sm_100a) implementation
+ * of LARA's grouped-query streaming-attention path.
+ *
+ * The reference drives its FPGA through a Python/PYNQ driver
+ * (sw/attn_driver.py): MMIO writes to CSRs, DMA of K/V per GQA group and of
+ * padded Q tiles, a host poll loop, and a DMA read of O.  This library replaces
+ * that MMIO/DMA layer and the RTL datapath behind it.  Every entry point below
+ * names the reference interface it replaces.
+ *
+ * Conventions
+ *  - bf16 tensors are passed as raw uint16_t words (IEEE bf16 upper halves),
+ *    exactly as the reference passes them (sw/attn_driver.py:88-103).
+ *  - Layouts: decode queries q[B][Hq][D]; KV cache [B][Hkv][Lmax][D]; the
+ *    dense transaction keeps the reference's head-major q[Hq][L][D],
+ *    k/v[Hkv][L][D], o[Hq][L][D] (sw/attn_driver.py:487-490).
+ *  - Query head h belongs to KV group h / (Hq/Hkv)
+ *    (sw/board_performance.py:182-184).
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *    stream).  Stateless kernels are asynchronous and stream-ordered.
+ *  - Every function returns a status code (LARA_OK on success).  The text of
+ *    the most recent failure on the calling thread is returned by
+ *    lara_last_error_string().
+ *  - A context is not thread-safe; use one context per device per thread.
+ */
+#ifndef LARA_B200_H
+#define LARA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LARA_API __attribute__((visibility("default")))
+#else
+#define LARA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  0x00-0x12 mirror the accelerator's ERROR_CODE CSR values
+ * (sw/attn_driver.py:80-85, hw/rtl/pkg/attn_pkg.sv:279-286). */
+#define LARA_OK 0x00              /* ERR_NONE */
+#define LARA_ERR_BAD_CFG 0x01     /* ERR_BAD_CFG: geometry / length / position out of range */
+#define LARA_ERR_BUSY_START 0x02  /* ERR_BUSY_START: context closed or busy */
+#define LARA_ERR_STREAM_LEN 0x10  /* ERR_STREAM_LEN: a tensor size does not match the configuration */
+#define LARA_ERR_STREAM_DEST 0x11 /* ERR_STREAM_DEST: null or misaligned buffer */
+#define LARA_ERR_RESULT_LEN 0x12  /* ERR_RESULT_LEN: output buffer too small */
+#define LARA_ERR_CUDA 0x20        /* a CUDA runtime call failed */
+#define LARA_ERR_TIMEOUT 0x21     /* a bounded device wait or lara_sync timed out */
+#define LARA_ERR_UNSUPPORTED 0x22 /* no kernel compiled for this head geometry */
+#define LARA_ERR_DEVICE 0x23      /* the kernel reported a device-side error status */
+
+#define LARA_ABI_VERSION 1
+
+LARA_API int lara_abi_version(void);
+LARA_API const char* lara_last_error_string(void);
+LARA_API const char* lara_status_name(int status);
+
+/* ------------------------------------------------------------------------ */
+/* Stateless kernels: caller-owned device memory (e.g. torch tensors).       */
+/* ------------------------------------------------------------------------ */
+
+/* Split plan for a decode workload on the current device.  lens_host may be
+ * NULL (every sequence is max_seq_len long) or point to B host int32 lengths.
+ * Writes the split count (grid.x) and tokens per split. */
+LARA_API int lara_decode_plan(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len,
+                     const int32_t* lens_host, int* num_splits, int* chunk_tokens);
+
+/* Bytes of device workspace a decode with `num_splits` splits needs. */
+LARA_API size_t lara_decode_workspace_bytes(int batch, int n_q_heads, int n_kv_heads, int head_dim, int num_splits);
+
+/* Zero a workspace (once, before its first use; kernels leave it reusable). */
+LARA_API int lara_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Read and clear the device status word of a workspace (synchronises the
+ * stream).  *device_status receives the raw bits (0 = no error). */
+LARA_API int lara_workspace_status(void* workspace, void* stream, int* device_status);
+
+/* One decode step: for every sequence b and query head h,
+ *   o[b,h,:] = softmax(scale * q[b,h,:] . K[b,h/G,:len_b,:]^T) . V[b,h/G,:len_b,:]
+ * bf16 in, exact products, fp32 accumulation and online softmax, bf16 RNE out.
+ * seq_lens: device int32[B], each in [0, max_seq_len]; a sequence of length 0
+ * gives a zero output.  num_splits/chunk_tokens come from lara_decode_plan
+ * (num_splits * chunk_tokens >= max_seq_len); pass 0/0 to plan here.
+ * Replaces: AttentionAccelerator.run_attention (sw/attn_driver.py:469-550)
+ * and the datapath it drives (hw/rtl/attn_top.sv:301-625) for one query token
+ * per sequence over a resident cache. */
+LARA_API int lara_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* seq_lens,
+                    uint16_t* o, int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len,
+                    float scale, int num_splits, int chunk_tokens, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Same as lara_gqa_decode but writes the unnormalised partial state of every
+ * (b, h) row instead of bf16 output: part_ml[(b*Hq+h)*2 + {0,1}] = {m, l}
+ * (m is the running max of scale*log2(e)*q.k, l the sum of 2^(s-m)) and
+ * part_acc[(b*Hq+h)*D + d] = sum 2^(s-m) v.  Used when a sequence is split
+ * across GPUs; lara_lse_combine merges the partials.  (The reference has a
+ * single device and no counterpart; this is the per-device half of
+ * split-KV decode.) */
+LARA_API int lara_gqa_decode_partial(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                            const int32_t* seq_lens, float* part_ml, float* part_acc, int batch, int n_q_heads,
+                            int n_kv_heads, int head_dim, int max_seq_len, float scale, int num_splits,
+                            int chunk_tokens, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Merge num_parts partial states of `rows` query rows:
+ * part_ml[(i*rows + r)*2 + {0,1}], part_acc[(i*rows + r)*D + d] -> o[r*D + d]
+ * (bf16 RNE; a row whose l sums to 0 gives zeros).
+ * Replaces: the O normalise + writeback of hw/rtl/mem/output_buffer.sv:271-286
+ * for state that was accumulated on several devices. */
+LARA_API int lara_lse_combine(const float* part_ml, const float* part_acc, int num_parts, int rows, int head_dim,
+                     uint16_t* o, void* stream);
+
+/* Append n_new tokens per sequence: k_new/v_new[B][Hkv][n_new][D] are written
+ * at positions seq_lens[b] .. seq_lens[b]+n_new-1 of the cache, then
+ * seq_lens[b] += n_new.  Rows that would pass max_seq_len are dropped and
+ * flag LARA_ERR_DEVICE in the workspace status (if workspace != NULL).
+ * Replaces: the K/V cache loads of sw/attn_driver.py:418-422 into
+ * hw/rtl/mem/kv_cache_ram.sv:45-91. */
+LARA_API int lara_kv_append(uint16_t* k_cache, uint16_t* v_cache, int32_t* seq_lens, const uint16_t* k_new,
+                   const uint16_t* v_new, int batch, int n_kv_heads, int head_dim, int max_seq_len, int n_new,
+                   void* workspace, void* stream);
+
+/* fp32 -> bf16 RNE words with the integer steps of the reference packer, so
+ * results (NaN and Inf patterns included) are bit-identical to it.
+ * src 16-byte aligned, dst 8-byte aligned.
+ * Replaces: fp32_to_bf16_u16 (sw/attn_driver.py:88-98). */
+LARA_API int lara_pack_bf16(const float* src, uint16_t* dst, size_t n, void* stream);
+
+/* Chunked prefill over the cache ("cache + self"): the n_new new tokens of
+ * every sequence are already appended (lara_kv_append) at positions
+ * cached_lens[b] .. cached_lens[b]+n_new-1, where cached_lens[b] (device
+ * int32[B]) is the length BEFORE the append.  q/o are token-major
+ * [B][n_new][Hq][D].  Query i of sequence b sits at position cached_lens[b]+i;
+ * with causal != 0 it sees tokens 0..cached_lens[b]+i (kv_pos <= q_pos,
+ * sw/board_performance.py:174-177), otherwise all cached_lens[b]+n_new.
+ * Workspace: lara_prefill_workspace_bytes.
+ * Replaces: run_attention's causal Q-tile x KV-tile traversal with causal tile
+ * skipping (hw/rtl/core/attn_core.sv:107-154) over a resident cache. */
+LARA_API size_t lara_prefill_workspace_bytes(int batch, int n_new, int n_q_heads, int n_kv_heads, int head_dim,
+                                             int max_seq_len);
+LARA_API int lara_gqa_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                              const int32_t* cached_lens, uint16_t* o, int batch, int n_new, int n_q_heads,
+                              int n_kv_heads, int head_dim, int max_seq_len, int causal, float scale,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* One dense attention transaction, the semantics of run_attention with
+ * Lq == Lkv == seq_len: q[Hq][L][D], k/v[Hkv][L][D], o[Hq][L][D] (device
+ * pointers).  Query i has position q_pos_base+i, key j kv_pos_base+j; with
+ * causal != 0 a key is visible when kv_pos <= q_pos
+ * (sw/board_performance.py:174-177).  A query row with no visible key gives
+ * zeros.  Workspace: lara_dense_workspace_bytes.
+ * Replaces: AttentionAccelerator.run_attention (sw/attn_driver.py:469-550). */
+LARA_API size_t lara_dense_workspace_bytes(int n_q_heads, int n_kv_heads, int head_dim, int seq_len);
+LARA_API int lara_attention_dense(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o, int n_q_heads,
+                         int n_kv_heads, int head_dim, int seq_len, int q_pos_base, int kv_pos_base, int causal,
+                         float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Context API: the backing of the Python AttentionAccelerator.  The context */
+/* owns the HBM KV cache, device I/O buffers, a stream and timing events.   */
+/* Tensor pointers are host memory unless on_device != 0.                    */
+/* ------------------------------------------------------------------------ */
+
+typedef struct lara_ctx lara_ctx;
+
+typedef struct lara_perf {
+  /* Device time of the last transaction in ns (clock_mhz = 1000, so these
+   * are "cycles" of a 1 GHz clock): total = first H2D copy to last D2H copy,
+   * mac = attention kernels, stall = host<->device copies. */
+  uint64_t cycles;
+  uint64_t mac_cycles;
+  uint64_t stall_cycles;
+  double clock_mhz;
+} lara_perf;
+
+/* Replaces: AttentionAccelerator.__init__ (Overlay load, buffer allocation;
+ * sw/attn_driver.py:251-288). */
+LARA_API int lara_create(int device, lara_ctx** out);
+
+/* Replaces: AttentionAccelerator.close (sw/attn_driver.py:324-331).  Frees
+ * every device and pinned buffer; NULL is accepted. */
+LARA_API int lara_destroy(lara_ctx* ctx);
+
+/* Head geometry and cache capacity; (re)allocates the KV cache and buffers,
+ * and empties the cache.  Defaults after lara_create: batch 1, 32/8 heads,
+ * head_dim 128, max_seq_len 512 (hw/rtl/pkg/attn_pkg.sv:172-176).
+ * Extension of the reference call surface (no CSR counterpart: the RTL
+ * geometry is fixed at synthesis). */
+LARA_API int lara_configure_heads(lara_ctx* ctx, int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len);
+
+/* Transaction registers of the dense path.  Replaces: configure
+ * (sw/attn_driver.py:364-376: SEQ_LEN, Q/KV_POS_BASE, CFG.causal) with its
+ * validation (1 <= seq_len <= max_seq_len, positions + seq_len <= 2^16). */
+LARA_API int lara_configure(lara_ctx* ctx, int seq_len, int q_pos_base, int kv_pos_base, int causal);
+
+/* Load the cache: k/v[B][Hkv][src_len][D], lens[B] (host int32, each <=
+ * src_len and <= max_seq_len).  Replaces: the KV_LOAD_REQ service of
+ * sw/attn_driver.py:418-422. */
+LARA_API int lara_kv_load(lara_ctx* ctx, const uint16_t* k, const uint16_t* v, const int32_t* lens, int src_len,
+                 int on_device);
+
+/* Append one chunk of n_new tokens per sequence (k/v[B][Hkv][n_new][D]). */
+LARA_API int lara_kv_append_ctx(lara_ctx* ctx, const uint16_t* k_new, const uint16_t* v_new, int n_new, int on_device);
+
+/* Chunked prefill: append k/v_new[B][Hkv][n_new][D], then attend
+ * q[B][n_new][Hq][D] -> o[B][n_new][Hq][D] over cache + self (see
+ * lara_gqa_prefill); synchronous. */
+LARA_API int lara_run_prefill_chunk(lara_ctx* ctx, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
+                                    uint16_t* o, int n_new, int causal, int on_device);
+
+/* Copy the current lengths (host int32[B]). */
+LARA_API int lara_get_seq_lens(lara_ctx* ctx, int32_t* lens_out);
+
+/* Decode: q[B][Hq][D] -> o[B][Hq][D] over the resident cache; synchronous
+ * (returns after o is written).  Replaces: run_attention's request service and
+ * readback (sw/attn_driver.py:418-464) for one query token per sequence. */
+LARA_API int lara_run_query(lara_ctx* ctx, const uint16_t* q, uint16_t* o, int on_device);
+
+/* Dense transaction with the configure()d registers: q[Hq][L][D],
+ * k/v[Hkv][L][D] -> o[Hq][L][D]; synchronous.  Replaces: run_attention
+ * (sw/attn_driver.py:469-550). */
+LARA_API int lara_run_attention(lara_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
+                       int on_device);
+
+/* Replaces: read_perf (sw/attn_driver.py:466-467, CSRs 0x100/0x108/0x10C). */
+LARA_API int lara_read_perf(lara_ctx* ctx, lara_perf* out);
+
+/* Wait for the context's stream; LARA_ERR_TIMEOUT after timeout_ms (< 0:
+ * no limit).  Replaces: wait_done's deadline (sw/attn_driver.py:442-454). */
+LARA_API int lara_sync(lara_ctx* ctx, int timeout_ms);
+
+/* Device the context was created on. */
+LARA_API int lara_ctx_device(lara_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LARA_B200_H */

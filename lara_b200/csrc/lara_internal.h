@@ -1,0 +1,89 @@
+// Internal (C++) interfaces shared by the CUDA translation units of
+// liblara_b200.so.  Nothing here is part of the C ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace lara {
+
+// Device status word bits (atomicOr'd into the first word of a workspace).
+enum DeviceStatus : int {
+  kDevOk = 0,
+  kDevWaitTimeout = 1 << 0,    // a bounded mbarrier wait gave up
+  kDevBadLength = 1 << 1,      // a sequence length was outside [0, max_seq_len]
+  kDevAppendOverflow = 1 << 2, // an appended row would pass max_seq_len
+};
+
+// One decode launch: queries of `batch` sequences (or of `batch` query rows
+// that share one K/V stream, for the dense transaction) against a bf16 KV
+// cache.  All strides are in elements; rows of K/V are `head_dim` contiguous
+// bf16 words, tokens of one (sequence, kv head) are contiguous.
+struct DecodeParams {
+  const uint16_t* q;   // q[b * q_sb + h * q_sh + d]
+  long long q_sb, q_sh;
+  const uint16_t* k;   // k[b * kv_sb + kvh * kv_sh + tok * D + d]
+  const uint16_t* v;
+  long long kv_sb, kv_sh;
+  uint16_t* o;         // o[b * o_sb + h * o_sh + d] (bf16), unused in partial mode
+  long long o_sb, o_sh;
+  // Rows: blockIdx.z = r is a query row; its K/V stream is sequence
+  // r / rows_per_seq, and it sees the first
+  //   clamp((lens ? lens[r / rows_per_seq] : 0) + len_c0 + len_c1 * (r % rows_per_seq), 0, max_seq_len)
+  // tokens.  Decode: rows_per_seq = 1, c0 = c1 = 0.  Dense transaction: one
+  // shared K/V (kv_sb = 0), rows_per_seq = L, c0/c1 from the causal rule.
+  // Chunked prefill: rows_per_seq = n new tokens, lens = cached lengths.
+  const int32_t* lens;
+  int len_c0, len_c1;
+  int rows_per_seq;
+  int max_seq_len;     // tokens allocated per (sequence, kv head) row
+  int batch;           // query rows (grid.z)
+  int n_q_heads, n_kv_heads, head_dim;
+  float scale_log2;    // softmax scale * log2(e)
+  int chunk;           // tokens per CTA (multiple of the kernel's tile)
+  int nsplit;          // grid.x; partial slots per row in the workspace
+  // workspace (see decode_workspace_layout)
+  int* status;
+  int* counters;       // [batch * n_kv_heads] (rows), zero between launches
+  float* part_ml;      // [batch * n_q_heads * nsplit * 2]
+  float* part_acc;     // [batch * n_q_heads * nsplit * head_dim]
+  // partial-output mode (split-KV across GPUs): when out_acc != nullptr the
+  // kernel writes unnormalised (m (log2 domain), l, acc[D]) per (b, h) row
+  // instead of bf16 output.
+  float* out_ml;       // [batch * n_q_heads * 2]
+  float* out_acc;      // [batch * n_q_heads * head_dim]
+};
+
+struct WorkspaceLayout {
+  size_t status_off, counters_off, ml_off, acc_off, total;
+};
+
+WorkspaceLayout decode_workspace_layout(int batch, int n_q_heads, int n_kv_heads, int head_dim, int nsplit);
+
+// Chooses the split count for a (batch, kv heads, max tokens) workload on the
+// current device.  `lens_host` (optional, [batch]) are the actual lengths; a
+// ragged batch is planned by token count instead of by waves.  Returns the
+// number of splits (grid.x) and the chunk in tokens; nsplit*chunk >= max_tokens.
+void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max_tokens, const int32_t* lens_host,
+                 int* nsplit, int* chunk);
+
+// Tile size (tokens per pipeline stage) of the compiled kernel for a head
+// geometry, or 0 when no kernel is compiled for it.
+int decode_tile_tokens(int head_dim, int group);
+
+cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream);
+
+cudaError_t lse_combine_launch(const float* part_ml, const float* part_acc, int num_parts, long long part_stride_rows,
+                               int rows, int head_dim, uint16_t* o, float* out_ml, float* out_acc,
+                               cudaStream_t stream);
+
+cudaError_t kv_append_launch(uint16_t* k_cache, uint16_t* v_cache, int32_t* lens, const uint16_t* k_new,
+                             const uint16_t* v_new, int batch, int n_kv_heads, int head_dim, int max_seq_len,
+                             int n_new, int* status, cudaStream_t stream);
+
+cudaError_t pack_bf16_launch(const float* src, uint16_t* dst, size_t n, cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace lara

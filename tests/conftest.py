@@ -1,0 +1,32 @@
+"""Shared pytest configuration: the ``gpu`` marker and fixture helpers."""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+GOLDEN = ROOT / "tests" / "golden"
+if str(GOLDEN) not in sys.path:
+    sys.path.insert(0, str(GOLDEN))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) CUDA device")
+    config.addinivalue_line("markers", "slow: full-size parity cases")
+
+
+def pytest_collection_modifyitems(config, items):
+    # GPU tests must never silently pass without a device: if a GPU test is
+    # selected on a machine without CUDA, it is an error, not a skip.
+    pass
+
+
+@pytest.fixture(scope="session")
+def golden_dir() -> Path:
+    return GOLDEN

@@ -1,0 +1,277 @@
+"""GPU parity of the decode path (C ABI through ``lara_b200.ops``) vs the CPU oracle.
+
+Tolerance: <= 2 bf16 ulp of the golden model's bf16 result per element, ulp
+floored at 2**-8 of the head vector's largest magnitude (``tests/parity.py``),
+and the same bound against the fp64 reference.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import oracle  # noqa: E402
+from parity import assert_bf16_parity, words_of  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    from lara_b200 import ops  # noqa: F401  (loads liblara_b200.so)
+
+    return torch.device("cuda:0")
+
+
+def _rand_words(g, shape, dev, std=1.0):
+    return (torch.randn(shape, generator=g, device=dev) * std).to(torch.bfloat16)
+
+
+def _run_case(dev, B, Hq, Hkv, D, lens, cap, *, seed=0, std=1.0, splits=(0, 0), boost=None):
+    from lara_b200 import ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    q = _rand_words(g, (B, Hq, D), dev, std)
+    k = _rand_words(g, (B, Hkv, cap, D), dev, std)
+    v = _rand_words(g, (B, Hkv, cap, D), dev, std)
+    if boost is not None:
+        k[..., :4] = (k[..., :4].float() * boost).to(torch.bfloat16)
+    lens_t = torch.tensor(lens, dtype=torch.int32, device=dev)
+    dec = ops.Decoder(B, Hq, Hkv, D, cap, dev, lens=np.asarray(lens), num_splits=splits[0],
+                      chunk_tokens=splits[1])
+    o = dec(q, k, v, lens_t)
+    torch.cuda.synchronize()
+    assert ops.workspace_status(dec.workspace) == 0
+    qw, kw, vw = words_of(q), words_of(k), words_of(v)
+    gold = oracle.decode_attention(qw, kw, vw, np.asarray(lens))
+    g64 = oracle.decode_attention_fp64(qw, kw, vw, np.asarray(lens))
+    return words_of(o), gold, g64, dec
+
+
+GEOMS = [
+    # (B, Hq, Hkv, D)
+    (2, 8, 2, 64),    # config-1 geometry (G=4, D=64)
+    (3, 32, 8, 128),  # Llama-3-8B geometry (G=4)
+    (2, 64, 8, 128),  # config-3 geometry (G=8)
+    (2, 8, 8, 128),   # MHA (G=1)
+    (2, 16, 8, 64),   # G=2, D=64
+    (2, 16, 2, 64),   # G=8, D=64
+    (1, 8, 4, 128),   # G=2
+    (1, 8, 8, 64),    # G=1, D=64
+]
+
+
+@pytest.mark.parametrize("geom", GEOMS, ids=lambda g: "B{}_Hq{}_Hkv{}_D{}".format(*g))
+def test_decode_geometries_ragged(dev, geom):
+    B, Hq, Hkv, D = geom
+    cap = 700
+    lens = [cap, 1, 333, 64, 65][:B] if B <= 5 else [cap] * B
+    o, gold, g64, _ = _run_case(dev, B, Hq, Hkv, D, lens, cap, seed=B * 100 + Hq)
+    assert_bf16_parity(o, gold, g64, what=str(geom))
+
+
+@pytest.mark.parametrize("splits", [(1, 4096), (4, 1024), (64, 64), (7, 640)])
+def test_decode_forced_splits(dev, splits):
+    """Split-KV merge inside the kernel (last-arriving CTA) for several plans."""
+    B, Hq, Hkv, D, cap = 2, 32, 8, 128, 4096
+    lens = [4096, 2999]
+    o, gold, g64, _ = _run_case(dev, B, Hq, Hkv, D, lens, cap, seed=7, std=0.5, splits=splits)
+    assert_bf16_parity(o, gold, g64, what=f"splits={splits}")
+
+
+def test_decode_repeat_is_deterministic_and_counters_reset(dev):
+    from lara_b200 import ops
+
+    B, Hq, Hkv, D, cap = 2, 32, 8, 128, 2048
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    q = _rand_words(g, (B, Hq, D), dev)
+    k = _rand_words(g, (B, Hkv, cap, D), dev)
+    v = _rand_words(g, (B, Hkv, cap, D), dev)
+    lens = torch.tensor([cap, 1500], dtype=torch.int32, device=dev)
+    dec = ops.Decoder(B, Hq, Hkv, D, cap, dev, num_splits=8, chunk_tokens=256)
+    outs = [dec(q, k, v, lens).clone() for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    ctr = dec.workspace[256:256 + 4 * B * Hkv].view(torch.int32)
+    assert int(ctr.abs().sum()) == 0
+
+
+def test_decode_zero_length_gives_zero(dev):
+    o, gold, _, _ = _run_case(dev, 3, 8, 2, 64, [0, 5, 0], 64, seed=11)
+    assert not np.any(o[0]) and not np.any(o[2])
+    assert_bf16_parity(o[1:2], gold[1:2])
+
+
+def test_decode_large_logits_stress(dev):
+    """Config-3 style: K channels 0..3 scaled by 20 (large logits)."""
+    o, gold, g64, _ = _run_case(dev, 2, 64, 8, 128, [4100, 777], 4100, seed=2, boost=20.0)
+    assert_bf16_parity(o, gold, g64, what="large logits")
+
+
+def test_decode_zero_inputs(dev):
+    from lara_b200 import ops
+
+    B, Hq, Hkv, D, cap = 2, 32, 8, 128, 300
+    z = torch.zeros((B, Hkv, cap, D), dtype=torch.bfloat16, device=dev)
+    q = torch.zeros((B, Hq, D), dtype=torch.bfloat16, device=dev)
+    o = ops.gqa_decode(q, z, z, torch.tensor([300, 17], dtype=torch.int32, device=dev))
+    assert not torch.any(o.view(torch.int16) != 0)
+
+
+def test_golden_cfg1_decode_with_append(dev, golden_dir):
+    """Config 1: 512 cached tokens, append 1 through the kernel, decode."""
+    from lara_b200 import ops
+
+    fx = np.load(golden_dir / "decode_cfg1.npz")
+    to_dev = lambda a: torch.from_numpy(a.astype(np.int16)).to(dev)  # noqa: E731
+    cap = 520
+    kc = torch.zeros((1, 2, cap, 64), dtype=torch.int16, device=dev)
+    vc = torch.zeros((1, 2, cap, 64), dtype=torch.int16, device=dev)
+    kc[:, :, :512] = to_dev(fx["k_cache"])
+    vc[:, :, :512] = to_dev(fx["v_cache"])
+    lens = torch.tensor([512], dtype=torch.int32, device=dev)
+    ops.kv_append(kc, vc, lens, to_dev(fx["k_new"])[:, :, None, :].contiguous(),
+                  to_dev(fx["v_new"])[:, :, None, :].contiguous())
+    assert int(lens.item()) == 513
+    q = to_dev(fx["q"])
+    o = ops.gqa_decode(q, kc, vc, lens)
+    ow = words_of(o)
+    e = assert_bf16_parity(ow, fx["o_fp32"], what="config 1 vs reference golden")
+    assert e["max_ulp_strict"] <= 2.0
+
+
+def test_kv_append_round_trip(dev):
+    """Appended rows land bit-exactly at seq_lens[b] and lengths advance."""
+    from lara_b200 import ops
+
+    B, Hkv, cap, D, n = 3, 4, 100, 128, 5
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    kc = _rand_words(g, (B, Hkv, cap, D), dev)
+    vc = _rand_words(g, (B, Hkv, cap, D), dev)
+    k0, v0 = kc.clone(), vc.clone()
+    lens = torch.tensor([0, 17, 95], dtype=torch.int32, device=dev)
+    kn = _rand_words(g, (B, Hkv, n, D), dev)
+    vn = _rand_words(g, (B, Hkv, n, D), dev)
+    ops.kv_append(kc, vc, lens, kn, vn)
+    torch.cuda.synchronize()
+    assert lens.tolist() == [5, 22, 100]
+    for b, start in enumerate([0, 17, 95]):
+        assert torch.equal(kc[b, :, start:start + n], kn[b])
+        assert torch.equal(vc[b, :, start:start + n], vn[b])
+        mask = torch.ones(cap, dtype=torch.bool, device=dev)
+        mask[start:start + n] = False
+        assert torch.equal(kc[b, :, mask], k0[b, :, mask])
+
+
+def test_kv_append_overflow_is_flagged(dev):
+    from lara_b200 import ops
+
+    kc = torch.zeros((1, 1, 8, 64), dtype=torch.bfloat16, device=dev)
+    lens = torch.tensor([6], dtype=torch.int32, device=dev)
+    kn = torch.ones((1, 1, 4, 64), dtype=torch.bfloat16, device=dev)
+    ws = ops.new_workspace(256, dev)
+    ops.kv_append(kc, kc.clone(), lens, kn, kn, workspace=ws)
+    assert ops.workspace_status(ws) != 0
+    assert int(lens.item()) == 8  # clamped at capacity, rows past it dropped
+
+
+def test_pack_bf16_matches_reference_kat(dev, golden_dir):
+    from lara_b200 import ops
+
+    kat = np.load(golden_dir / "kat_bf16.npz")
+    x = torch.from_numpy(kat["fp32_bits"].view(np.float32).copy()).to(dev)
+    got = ops.pack_bf16(x).cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(got, kat["bf16_words"])
+    # ragged tail lengths
+    for n in (1, 3, 5, 4099):
+        got = ops.pack_bf16(x[:n].contiguous()).cpu().numpy().view(np.uint16)
+        np.testing.assert_array_equal(got, kat["bf16_words"][:n])
+
+
+def test_partial_plus_lse_combine_equals_full(dev):
+    """Split a sequence into 4 KV shards (as 4 GPUs would), decode partials, combine."""
+    from lara_b200 import ops
+
+    B, Hq, Hkv, D, L, P = 2, 32, 8, 128, 4096, 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    q = _rand_words(g, (B, Hq, D), dev, 0.5)
+    k = _rand_words(g, (B, Hkv, L, D), dev, 0.5)
+    v = _rand_words(g, (B, Hkv, L, D), dev, 0.5)
+    shard = L // P
+    mls, accs = [], []
+    for i in range(P):
+        ks = k[:, :, i * shard:(i + 1) * shard].contiguous()
+        vs = v[:, :, i * shard:(i + 1) * shard].contiguous()
+        lens = torch.full((B,), shard, dtype=torch.int32, device=dev)
+        dec = ops.Decoder(B, Hq, Hkv, D, shard, dev)
+        ml, acc = dec.partial(q, ks, vs, lens)
+        mls.append(ml)
+        accs.append(acc)
+    o = ops.lse_combine(torch.stack(mls), torch.stack(accs)).view(B, Hq, D)
+    qw, kw, vw = words_of(q), words_of(k), words_of(v)
+    gold = oracle.decode_attention(qw, kw, vw, np.full(B, L))
+    assert_bf16_parity(words_of(o), gold, oracle.decode_attention_fp64(qw, kw, vw, np.full(B, L)), what="combine")
+
+
+def test_rejects_bad_geometry(dev):
+    from lara_b200 import ops
+
+    q = torch.zeros((1, 12, 128), dtype=torch.bfloat16, device=dev)
+    k = torch.zeros((1, 5, 16, 128), dtype=torch.bfloat16, device=dev)
+    with pytest.raises(ValueError):
+        ops.gqa_decode(q, k, k, torch.tensor([16], dtype=torch.int32, device=dev))
+
+
+@pytest.mark.slow
+def test_config2_full_size_sampled(dev):
+    """Config 2 at full size (B=64, L=4096); oracle on 24 sampled (b, kv-head) pairs."""
+    from lara_b200 import ops
+    from lara_b200.workloads import CONFIGS, make_decode_inputs
+
+    cfg = CONFIGS[2]
+    q, k, v, lens = make_decode_inputs(cfg, dev)
+    dec = ops.Decoder(cfg.batch, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, cfg.seq_len, dev)
+    o = words_of(dec(q, k, v, lens))
+    rng = np.random.default_rng(0)
+    pairs = sorted({(int(b), int(h)) for b, h in zip(rng.integers(0, 64, 24), rng.integers(0, 8, 24))})
+    bs = sorted({b for b, _ in pairs})
+    qw = words_of(q)
+    G = cfg.group
+    for b in bs:
+        kw, vw = words_of(k[b:b + 1]), words_of(v[b:b + 1])
+        hs = [h for bb, h in pairs if bb == b]
+        gold = oracle.decode_attention(qw[b:b + 1], kw, vw, np.array([4096]), pairs=[(0, h) for h in hs])
+        g64 = oracle.decode_attention_fp64(qw[b:b + 1], kw, vw, np.array([4096]), pairs=[(0, h) for h in hs])
+        for h in hs:
+            sl = slice(h * G, (h + 1) * G)
+            assert_bf16_parity(o[b, sl], gold[0, sl], g64[0, sl], what=f"cfg2 b={b} kvh={h}")
+
+
+@pytest.mark.slow
+def test_config3_ragged_sampled(dev):
+    """Config 3 (ragged lengths, x20 K channels) on the first 16 sequences."""
+    from lara_b200 import ops
+    from lara_b200.workloads import CONFIGS, make_decode_inputs
+
+    cfg = CONFIGS[3]
+    B = 16
+    q, k, v, lens = make_decode_inputs(cfg, dev, batch=B)
+    cap = k.shape[2]
+    lens_np = lens.cpu().numpy()
+    dec = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, cap, dev, lens=lens_np)
+    o = words_of(dec(q, k, v, lens))
+    qw = words_of(q)
+    for b in range(0, B, 3):
+        n = int(lens_np[b])
+        kw, vw = words_of(k[b:b + 1, :, :n]), words_of(v[b:b + 1, :, :n])
+        gold = oracle.decode_attention(qw[b:b + 1], kw, vw, np.array([n]))
+        g64 = oracle.decode_attention_fp64(qw[b:b + 1], kw, vw, np.array([n]))
+        assert_bf16_parity(o[b:b + 1], gold, g64, what=f"cfg3 b={b} len={n}")

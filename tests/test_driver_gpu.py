@@ -1,0 +1,193 @@
+"""GPU tests of the drop-in driver (``lara_b200.attn_driver``) and the dense path.
+
+These replay what the reference harnesses do with ``AttentionAccelerator``:
+``board_test.py`` (zero in -> zero out, NPZ comparison), ``board_matrix.py`` /
+``board_performance.py`` (per-case ``run_attention``, ``save_last_profile``,
+``read_perf`` validity, ``bf16_u16_to_fp32`` on outputs).  Expected outputs
+are the reference's own ``cpu_attention_numpy`` results (fixture rows) and the
+pinned oracle (full outputs); tolerance as in ``tests/parity.py``.
+"""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import make_golden as mg  # noqa: E402
+import oracle  # noqa: E402
+from parity import assert_bf16_parity, words_of  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def accel():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    from lara_b200.attn_driver import AttentionAccelerator
+
+    a = AttentionAccelerator("lara_b200.bit")
+    yield a
+    a.close()
+
+
+@pytest.mark.parametrize("case", mg.BOARD_CASES, ids=lambda c: f"L{c[0]}_{'c' if c[1] else 'nc'}_q{c[2]}kv{c[3]}")
+def test_board_case_matrix(accel, golden_dir, case):
+    L, causal, qb, kb = case
+    name = f"board_L{L}_{'causal' if causal else 'noncausal'}_q{qb}_kv{kb}"
+    fx = np.load(golden_dir / f"{name}.npz")
+    q, k, v = mg.board_inputs(int(fx["seed"]), L, oracle.fp32_to_bf16_u16)
+    out = accel.run_attention(q, k, v, seq_len=L, causal=causal, q_pos_base=qb, kv_pos_base=kb)
+    assert out.dtype == np.uint16 and out.shape == (32, L, 128)
+    rows = fx["rows"]
+    # against the reference's own output rows
+    assert_bf16_parity(out[:, rows, :], fx["o_rows"], what=f"{name} vs reference rows")
+    # against the pinned oracle (full output) and fp64
+    gold = oracle.cpu_attention_numpy(q, k, v, causal=causal, q_pos_base=qb, kv_pos_base=kb)
+    assert_bf16_parity(out, gold, what=f"{name} vs oracle")
+    # harness invariants (sw/board_performance.py:345-378)
+    perf = accel.read_perf()
+    prof = accel.last_profile
+    assert prof is not None and prof.clock_mhz > 0 and perf["cycles"] > 0
+    assert 0 <= perf["mac_cycles"] <= perf["cycles"] and 0 <= perf["stall_cycles"] <= perf["cycles"]
+
+
+def test_zero_input_smoke(accel):
+    """sw/board_test.py:45-79: a zero transaction returns all-zero words."""
+    from lara_b200.attn_driver import HEAD_DIM, N_KV_HEADS, N_Q_HEADS
+
+    q = np.zeros((N_Q_HEADS, 16, HEAD_DIM), np.uint16)
+    k = np.zeros((N_KV_HEADS, 16, HEAD_DIM), np.uint16)
+    out = accel.run_attention(q, k, k, seq_len=16)
+    assert not np.any(out)
+
+
+def test_profile_round_trip(accel, tmp_path):
+    q, k, v = mg.board_inputs(5, 32, oracle.fp32_to_bf16_u16)
+    accel.run_attention(q, k, v, seq_len=32)
+    p = tmp_path / "profile.json"
+    accel.save_last_profile(p)
+    d = json.loads(p.read_text())
+    assert d["seq_len"] == 32 and d["clock_mhz"] == 1000.0 and d["pl_total_cycles"] > 0
+
+
+def test_fp32_inputs_are_packed(accel):
+    rng = np.random.default_rng(1)
+    qf = rng.standard_normal((32, 8, 128)).astype(np.float32)
+    kf = rng.standard_normal((8, 8, 128)).astype(np.float32)
+    vf = rng.standard_normal((8, 8, 128)).astype(np.float32)
+    out_f = accel.run_attention(qf, kf, vf, seq_len=8)
+    pk = oracle.fp32_to_bf16_u16
+    out_w = accel.run_attention(pk(qf), pk(kf), pk(vf), seq_len=8)
+    np.testing.assert_array_equal(out_f, out_w)
+
+
+def test_validation_errors(accel):
+    q = np.zeros((32, 4, 128), np.uint16)
+    k = np.zeros((8, 4, 128), np.uint16)
+    with pytest.raises(ValueError):
+        accel.run_attention(q, k, k, seq_len=0)
+    with pytest.raises(ValueError):
+        accel.run_attention(np.zeros((32, 513, 128), np.uint16), np.zeros((8, 513, 128), np.uint16),
+                            np.zeros((8, 513, 128), np.uint16))
+    with pytest.raises(ValueError):
+        accel.run_attention(q, k[:, :3], k, seq_len=4)
+    with pytest.raises(ValueError):
+        accel.configure(4, q_pos_base=65534)
+
+
+def test_dead_causal_rows_are_zero(accel):
+    """kv_pos_base beyond q positions: no visible key -> zeros (RTL l == 0 rule)."""
+    q, k, v = mg.board_inputs(8, 16, oracle.fp32_to_bf16_u16)
+    out = accel.run_attention(q, k, v, seq_len=16, causal=True, q_pos_base=0, kv_pos_base=8)
+    assert not np.any(out[:, :8])
+    gold = oracle.prefill_attention(q[None], k[None], v[None], np.array([16]), 0, causal=True, kv_pos_base=8)[0]
+    assert_bf16_parity(out[:, 8:], gold[:, 8:])
+
+
+def test_closed_accelerator_raises():
+    from lara_b200.attn_driver import AttentionAccelerator
+
+    a = AttentionAccelerator()
+    a.close()
+    a.close()  # idempotent
+    with pytest.raises(RuntimeError):
+        a.run_attention(np.zeros((32, 1, 128), np.uint16), np.zeros((8, 1, 128), np.uint16),
+                        np.zeros((8, 1, 128), np.uint16))
+    with pytest.raises(RuntimeError):
+        with a:
+            pass
+
+
+def test_decode_extension_cfg1(golden_dir):
+    """configure_heads / load_kv / append_kv / run_query on the config-1 golden step."""
+    from lara_b200.attn_driver import AttentionAccelerator
+
+    fx = np.load(golden_dir / "decode_cfg1.npz")
+    with AttentionAccelerator() as a:
+        a.configure_heads(8, 2, 64, max_seq_len=600, batch=1)
+        a.load_kv(fx["k_cache"], fx["v_cache"])
+        a.append_kv(fx["k_new"], fx["v_new"])
+        assert a.seq_lens.tolist() == [513]
+        o = a.run_query(fx["q"])
+        assert_bf16_parity(o, fx["o_fp32"], what="driver run_query cfg1")
+        np.testing.assert_array_equal(a.read_output(), o)
+        perf = a.read_perf()
+        assert 0 <= perf["mac_cycles"] <= perf["cycles"]
+
+
+def test_decode_extension_ragged_batch():
+    from lara_b200.attn_driver import AttentionAccelerator
+
+    rng = np.random.default_rng(4)
+    B, Hq, Hkv, D, L = 5, 32, 8, 128, 1000
+    pk = oracle.fp32_to_bf16_u16
+    k = pk(rng.standard_normal((B, Hkv, L, D)).astype(np.float32) * 0.5)
+    v = pk(rng.standard_normal((B, Hkv, L, D)).astype(np.float32) * 0.5)
+    q = pk(rng.standard_normal((B, Hq, D)).astype(np.float32) * 0.5)
+    lens = np.array([1000, 1, 513, 0, 64], np.int32)
+    with AttentionAccelerator() as a:
+        a.configure_heads(Hq, Hkv, D, max_seq_len=1024, batch=B)
+        a.load_kv(k, v, lens)
+        o = a.run_query(q)
+    gold = oracle.decode_attention(q, k, v, lens)
+    assert_bf16_parity(o, gold, what="ragged run_query")
+
+
+def test_prefill_chunk_extension():
+    from lara_b200.attn_driver import AttentionAccelerator
+
+    rng = np.random.default_rng(6)
+    B, Hq, Hkv, D, C, n = 2, 32, 8, 128, 300, 40
+    pk = oracle.fp32_to_bf16_u16
+    k = pk(rng.standard_normal((B, Hkv, C, D)).astype(np.float32) * 0.5)
+    v = pk(rng.standard_normal((B, Hkv, C, D)).astype(np.float32) * 0.5)
+    kn = pk(rng.standard_normal((B, Hkv, n, D)).astype(np.float32) * 0.5)
+    vn = pk(rng.standard_normal((B, Hkv, n, D)).astype(np.float32) * 0.5)
+    q = pk(rng.standard_normal((B, n, Hq, D)).astype(np.float32) * 0.5)
+    with AttentionAccelerator() as a:
+        a.configure_heads(Hq, Hkv, D, max_seq_len=512, batch=B)
+        a.load_kv(k, v, np.array([C, 250], np.int32))
+        o = a.run_prefill_chunk(q, kn, vn, causal=True)
+        assert a.seq_lens.tolist() == [C + n, 250 + n]
+    for b, c in enumerate([C, 250]):
+        k_all = np.concatenate([k[b:b + 1, :, :c], kn[b:b + 1]], axis=2)
+        v_all = np.concatenate([v[b:b + 1, :, :c], vn[b:b + 1]], axis=2)
+        gold = oracle.prefill_attention(q[b:b + 1].transpose(0, 2, 1, 3), k_all, v_all, np.array([c + n]), c,
+                                        causal=True)
+        assert_bf16_parity(o[b].transpose(1, 0, 2), gold[0], what=f"prefill b={b}")
+
+
+def test_dense_ops_matches_driver(accel):
+    from lara_b200 import ops
+
+    q, k, v = mg.board_inputs(12, 64, oracle.fp32_to_bf16_u16)
+    out = accel.run_attention(q, k, v, seq_len=64, causal=True, q_pos_base=31, kv_pos_base=7)
+    dev = torch.device("cuda:0")
+    t = lambda a: torch.from_numpy(a.astype(np.int16)).to(dev)  # noqa: E731
+    o2 = ops.attention_dense(t(q), t(k), t(v), causal=True, q_pos_base=31, kv_pos_base=7)
+    np.testing.assert_array_equal(words_of(o2), out)
