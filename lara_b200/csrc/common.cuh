@@ -60,6 +60,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of phase completion (acquire at CTA scope).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false (and never spins forever) if the phase with the
 // given parity has not completed within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
@@ -120,6 +133,23 @@ __device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
 __device__ __forceinline__ void bf16x4_to_f32(const uint2& u, float f[4]) {
   f[0] = bf16lo(u.x); f[1] = bf16hi(u.x);
   f[2] = bf16lo(u.y); f[3] = bf16hi(u.y);
+}
+
+// VEC bf16 words -> VEC/2 fp32 pairs (element 2i in .x, 2i+1 in .y)
+template <int VEC>
+__device__ __forceinline__ void load_bf16_pairs(const uint16_t* p, float2 f[VEC / 2]) {
+  if constexpr (VEC == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    f[0] = make_float2(bf16lo(u.x), bf16hi(u.x));
+    f[1] = make_float2(bf16lo(u.y), bf16hi(u.y));
+    f[2] = make_float2(bf16lo(u.z), bf16hi(u.z));
+    f[3] = make_float2(bf16lo(u.w), bf16hi(u.w));
+  } else {
+    static_assert(VEC == 4, "VEC must be 4 or 8");
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    f[0] = make_float2(bf16lo(u.x), bf16hi(u.x));
+    f[1] = make_float2(bf16lo(u.y), bf16hi(u.y));
+  }
 }
 
 // VEC (4 or 8) bf16 words -> fp32

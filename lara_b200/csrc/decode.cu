@@ -73,8 +73,8 @@ struct Traits {
   static constexpr int kCbufFloats = 2 * kWarps * G;
   static constexpr int kPbufOff = kBigBytes;
   static constexpr int kCbufOff = kPbufOff + kPbufFloats * 4;
-  static constexpr int kBarOff = (kCbufOff + kCbufFloats * 4 + 15) / 16 * 16;
-  static constexpr int kCntOff = kBarOff + kStages * 8;
+  static constexpr int kBarOff = (kCbufOff + kCbufFloats * 4 + 15) / 16 * 16;  // full[], empty[]
+  static constexpr int kCntOff = kBarOff + 2 * kStages * 8;                      // refill round per stage
   static constexpr int kFlagOff = kCntOff + kStages * 4;
   static constexpr int kSmemBytes = kFlagOff + 16;
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
@@ -149,7 +149,8 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   const int ntiles = (ntok + T::kTile - 1) / T::kTile;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::kBarOff);
-  int* arrivals = reinterpret_cast<int*>(smem + T::kCntOff);
+  uint64_t* empty = full + T::kStages;
+  int* refill_round = reinterpret_cast<int*>(smem + T::kCntOff);
   int* flag = reinterpret_cast<int*>(smem + T::kFlagOff);
   float* pbuf = reinterpret_cast<float*>(smem + T::kPbufOff);
   float* cbuf = reinterpret_cast<float*>(smem + T::kCbufOff);
@@ -162,7 +163,8 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   if (threadIdx.x == 0) {
     for (int s = 0; s < T::kStages; ++s) {
       mbar_init(&full[s], 1);
-      arrivals[s] = 0;
+      mbar_init(&empty[s], T::kWarps);
+      refill_round[s] = 0;
     }
     flag[0] = 0;  // error
     flag[1] = 0;  // last-CTA broadcast
@@ -182,22 +184,24 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   const int my_tw = my_it * T::kTPI + half;   // token (within the warp slice) of that score
   const bool dup_writer = (c & ((1 << T::kR) - 1)) == 0;
   const bool head_writer = dup_writer && lane < (G << T::kR);  // one lane per head, pass 0, row 0
+  constexpr int V2 = V / 2;
 
-  float qf[G][V];
+  float2 qp[G][V2];
 #pragma unroll
   for (int g = 0; g < G; ++g)
-    load_bf16_vec<V>(p.q + b * p.q_sb + (long long)(kvh * G + g) * p.q_sh + c * V, qf[g]);
-  float acc[G][V];
+    load_bf16_pairs<V>(p.q + b * p.q_sb + (long long)(kvh * G + g) * p.q_sh + c * V, qp[g]);
+  float2 acc[G][V2];
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int e = 0; e < V; ++e) acc[g][e] = 0.f;
+    for (int j = 0; j < V2; ++j) acc[g][j] = make_float2(0.f, 0.f);
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
 
   for (int i = 0; i < ntiles; ++i) {
     const int st = i % T::kStages;
-    if (!mbar_wait_bounded(&full[st], (i / T::kStages) & 1)) {
+    const int round = i / T::kStages;
+    if (!mbar_wait_bounded(&full[st], round & 1)) {
       ok = false;
       break;
     }
@@ -205,19 +209,20 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     const uint8_t* Vt = Kt + T::kHalfStage;
     const int nvalid = min(T::kTile, ntok - i * T::kTile) - warp * T::kTokPerWarp;
 
-    // QK^T: ITER token rows x G heads of partial dot products over V dims.
+    // QK^T: ITER token rows x G heads of partial dot products over V dims,
+    // accumulated as (even, odd) dim pairs with packed fp32 FMA.
     float part[T::kNV];
 #pragma unroll
     for (int it = 0; it < T::kIter; ++it) {
       const int tw = it * T::kTPI + half;
-      float kf[V];
-      load_bf16_vec<V>(reinterpret_cast<const uint16_t*>(Kt + tw * T::kRowBytes) + c * V, kf);
+      float2 kp[V2];
+      load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Kt + tw * T::kRowBytes) + c * V, kp);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float a = qf[g][0] * kf[0];
+        float2 a2 = __fmul2_rn(qp[g][0], kp[0]);
 #pragma unroll
-        for (int e = 1; e < V; ++e) a = fmaf(qf[g][e], kf[e], a);
-        part[it * G + g] = a;
+        for (int j = 1; j < V2; ++j) a2 = __ffma2_rn(qp[g][j], kp[j], a2);
+        part[it * G + g] = a2.x + a2.y;
       }
     }
     // Reduce-scatter over the row's lanes: each step halves the values a lane
@@ -255,6 +260,8 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     for (int off = 1 << (T::kR + T::kLogG); off < 32; off <<= 1)
       tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
     l_run = l_run * corr + tsum;
+    // The accumulator needs rescaling only if some head's running max moved.
+    const bool moved = __any_sync(0xffffffffu, m_new != m_run);
     m_run = m_new;
 
     float* pb = pbuf + ((i & 1) * T::kWarps + warp) * (T::kTokPerWarp * G);
@@ -264,39 +271,54 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     __syncwarp();
 
     // P.V with the rescale of the running accumulator.
+    if (moved) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float cr = cb[g];
+      for (int g = 0; g < G; ++g) {
+        const float cr = cb[g];
+        const float2 cr2 = make_float2(cr, cr);
 #pragma unroll
-      for (int e = 0; e < V; ++e) acc[g][e] *= cr;
+        for (int j = 0; j < V2; ++j) acc[g][j] = __fmul2_rn(acc[g][j], cr2);
+      }
     }
 #pragma unroll
     for (int it = 0; it < T::kIter; ++it) {
       const int tw = it * T::kTPI + half;
       if (tw < nvalid) {
-        float vf[V];
-        load_bf16_vec<V>(reinterpret_cast<const uint16_t*>(Vt + tw * T::kRowBytes) + c * V, vf);
+        float2 vp[V2];
+        load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Vt + tw * T::kRowBytes) + c * V, vp);
+        float pg[G];
+        const float* prow = pb + tw * G;
+        if constexpr (G % 4 == 0) {
+#pragma unroll
+          for (int g = 0; g < G; g += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(prow + g);
+            pg[g] = f.x; pg[g + 1] = f.y; pg[g + 2] = f.z; pg[g + 3] = f.w;
+          }
+        } else if constexpr (G == 2) {
+          const float2 f = *reinterpret_cast<const float2*>(prow);
+          pg[0] = f.x; pg[1] = f.y;
+        } else {
+          pg[0] = prow[0];
+        }
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          const float pg = pb[tw * G + g];
+          const float2 p2 = make_float2(pg[g], pg[g]);
 #pragma unroll
-          for (int e = 0; e < V; ++e) acc[g][e] = fmaf(pg, vf[e], acc[g][e]);
+          for (int j = 0; j < V2; ++j) acc[g][j] = __ffma2_rn(p2, vp[j], acc[g][j]);
         }
       }
     }
-    // Release the stage.  The warp that completes the stage's arrivals
-    // refills it with tile i + kStages (no thread ever waits for this).
+    // Release the stage (mbarrier arrive: release semantics).  A warp that
+    // then observes the release complete (test_wait: acquire) claims the
+    // refill of tile i + kStages with one CAS; nobody blocks on it.
     __syncwarp();
     if (lane == 0) {
-      __threadfence_block();
-      const int prev = atomicAdd(&arrivals[st], 1);
-      if (prev == (i / T::kStages + 1) * T::kWarps - 1) {
-        __threadfence_block();
-        const int nxt = i + T::kStages;
-        if (nxt < ntiles) {
-          issue_tile<D, G>(smem, full, nxt, ntok, kg, vg, pol);
-          atomicMax(&flag[2], nxt + 1);
-        }
+      mbar_arrive(&empty[st]);
+      const int nxt = i + T::kStages;
+      if (nxt < ntiles && mbar_test_wait(&empty[st], round & 1) &&
+          atomicCAS(&refill_round[st], round, round + 1) == round) {
+        issue_tile<D, G>(smem, full, nxt, ntok, kg, vg, pol);
+        atomicMax(&flag[2], nxt + 1);
       }
     }
   }
@@ -307,7 +329,10 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
-      for (int e = 0; e < V; ++e) acc[g][e] += __shfl_xor_sync(0xffffffffu, acc[g][e], off);
+      for (int j = 0; j < V2; ++j) {
+        acc[g][j].x += __shfl_xor_sync(0xffffffffu, acc[g][j].x, off);
+        acc[g][j].y += __shfl_xor_sync(0xffffffffu, acc[g][j].y, off);
+      }
 
   if (!ok) atomicExch(&flag[0], 1);
   __syncthreads();
@@ -330,9 +355,9 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
 #pragma unroll
     for (int g = 0; g < G; ++g)
 #pragma unroll
-      for (int e = 0; e < V; e += 4)
-        *reinterpret_cast<float4*>(aw + (warp * G + g) * D + c * V + e) =
-            make_float4(acc[g][e], acc[g][e + 1], acc[g][e + 2], acc[g][e + 3]);
+      for (int j = 0; j < V2; j += 2)
+        *reinterpret_cast<float4*>(aw + (warp * G + g) * D + c * V + 2 * j) =
+            make_float4(acc[g][j].x, acc[g][j].y, acc[g][j + 1].x, acc[g][j + 1].y);
   }
   if (head_writer) {
     mw[warp * G + my_g] = m_run;
@@ -489,10 +514,9 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
   const int tile = k.tile > 0 ? k.tile : 64;
   const int L = max_tokens < 1 ? 1 : max_tokens;
   const int cps = k.fn ? occupancy(k) : 1;
-  const long long slots = (long long)device_sm_count() * cps;
   // Tokens of latency a CTA spends before its stream runs (exposed when the
   // SM holds a single CTA, mostly hidden behind a neighbour otherwise).
-  const double ovh = (cps > 1 ? 0.5 : 2.0) * tile;
+  const double ovh = 2.0 * tile;
   bool uniform = true;
   long long total = 0;
   if (lens_host) {
@@ -510,17 +534,23 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
     const int chunk = ((max_tiles + s - 1) / s) * tile;
     const int s_eff = (L + chunk - 1) / chunk;
     double cost;
+    // Bandwidth-bound: the step ends when the SM with the most tokens to
+    // stream is done; every CTA adds ~ovh tokens of prologue/epilogue.
+    const long long sms = device_sm_count();
     if (uniform) {
       const int len0 = lens_host ? (lens_host[0] < 1 ? 1 : lens_host[0]) : L;
       const long long ctas = (long long)batch * n_kv_heads * ((len0 + chunk - 1) / chunk);
-      const long long waves = (ctas + slots - 1) / slots;
+      const long long per_sm = (ctas + sms - 1) / sms;
       const int per = len0 < chunk ? len0 : chunk;
-      cost = (double)waves * (per + ovh);
+      // An SM running a single CTA streams at about 70% of the rate it
+      // reaches with two resident CTAs (measured on B200, config 2 sweeps).
+      const double single = (ctas < sms * (long long)(cps > 1 ? 2 : 1)) ? 0.7 : 1.0;
+      cost = (double)per_sm * (per + ovh) / single;
     } else {
       long long ctas = 0;
       for (int b = 0; b < batch; ++b) ctas += (lens_host[b] + chunk - 1) / chunk;
       ctas *= n_kv_heads;
-      cost = ((double)total * n_kv_heads + (double)ctas * ovh) / (double)slots + 0.5 * chunk;
+      cost = ((double)total * n_kv_heads + (double)ctas * ovh) / (double)sms + 0.5 * chunk;
     }
     if (cost < best * (1.0 - 1e-6)) {
       best = cost;

@@ -13,6 +13,9 @@ were produced by importing the reference's own ``cpu_attention_numpy``
 """
 
 from .attention import (  # noqa: F401
+    PARITY_FLOOR_FRAC,
+    PARITY_ULPS,
+    bf16_parity_error,
     bf16_u16_to_fp32,
     bf16_ulp,
     cpu_attention_numpy,

@@ -76,6 +76,46 @@ def ulp_distance(actual_words: np.ndarray, expected_words: np.ndarray) -> np.nda
     return np.abs(a - e) / bf16_ulp(expected_words)
 
 
+# Parity tolerance of the B200 kernels (<= 2 bf16 ulp of
+# the golden model's result).  The ulp is taken at each golden element's
+# magnitude, floored at 2**-8 of the largest magnitude in the same output
+# vector (the last axis: one query head's D values), because near-zero
+# elements produced by cancellation carry an fp32 rounding error that scales
+# with the vector, and the golden model and the kernel both accumulate in
+# fp32, in different orders.
+PARITY_ULPS = 2.0
+PARITY_FLOOR_FRAC = 2.0 ** -8
+
+
+def _ulp_at(mag: np.ndarray) -> np.ndarray:
+    m = np.maximum(np.asarray(mag, dtype=np.float64), 2.0 ** -126)
+    return np.ldexp(1.0, (np.floor(np.log2(m)) - 7).astype(np.int64))
+
+
+def bf16_parity_error(actual_words: np.ndarray, golden: np.ndarray) -> dict:
+    """Error of bf16 words against golden values (fp32 or fp64), in bf16 ulp.
+
+    ``max_ulp`` uses the floored ulp above (the pass criterion is
+    ``max_ulp <= PARITY_ULPS``); ``max_ulp_strict`` uses no floor.
+    """
+    golden_words = fp32_to_bf16_u16(np.asarray(golden, dtype=np.float32))
+    g = bf16_u16_to_fp32(golden_words).astype(np.float64)
+    a = bf16_u16_to_fp32(np.asarray(actual_words, dtype=np.uint16)).astype(np.float64)
+    err = np.abs(a - g)
+    if err.size == 0:
+        return {"max_ulp": 0.0, "max_ulp_strict": 0.0, "n_over_strict": 0, "n": 0, "finite": True}
+    row_max = np.max(np.abs(g), axis=-1, keepdims=True)
+    floored = _ulp_at(np.maximum(np.abs(g), PARITY_FLOOR_FRAC * row_max))
+    strict = _ulp_at(np.abs(g))
+    return {
+        "max_ulp": float(np.max(err / floored)),
+        "max_ulp_strict": float(np.max(err / strict)),
+        "n_over_strict": int(np.count_nonzero(err > PARITY_ULPS * strict)),
+        "n": int(err.size),
+        "finite": bool(np.all(np.isfinite(a))),
+    }
+
+
 # ---------------------------------------------------------------------------
 # attention restatements
 # ---------------------------------------------------------------------------
