@@ -542,10 +542,11 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
       const long long ctas = (long long)batch * n_kv_heads * ((len0 + chunk - 1) / chunk);
       const long long per_sm = (ctas + sms - 1) / sms;
       const int per = len0 < chunk ? len0 : chunk;
-      // An SM running a single CTA streams at about 70% of the rate it
-      // reaches with two resident CTAs (measured on B200, config 2 sweeps).
-      const double single = (ctas < sms * (long long)(cps > 1 ? 2 : 1)) ? 0.7 : 1.0;
-      cost = (double)per_sm * (per + ovh) / single;
+      // The busiest SM runs its CTAs `cps` at a time; a CTA left running
+      // alone streams at about 70% of the SM's two-CTA rate (measured on
+      // B200 in config-2 split sweeps).
+      const long long alone = cps > 1 ? per_sm % cps : 0;
+      cost = (double)(per_sm - alone) * (per + ovh) + (double)alone * (per + ovh) / 0.7;
     } else {
       long long ctas = 0;
       for (int b = 0; b < batch; ++b) ctas += (lens_host[b] + chunk - 1) / chunk;
