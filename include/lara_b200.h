@@ -157,6 +157,33 @@ LARA_API int lara_attention_dense(const uint16_t* q, const uint16_t* k, const ui
                          int n_kv_heads, int head_dim, int seq_len, int q_pos_base, int kv_pos_base, int causal,
                          float scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode with no allocation by the caller or the library.  Same arguments,
+ * semantics and results as lara_gqa_decode, minus the workspace: the split
+ * partials, arrival counters and status word live in a fixed array of
+ * LARA_NOALLOC_SCRATCH_BYTES in the library's own device memory, reserved on
+ * every GPU that loads the library until the process exits.  For callers that
+ * cannot allocate device memory where they run attention (a plugin inside a
+ * framework that owns all device allocations, a serving loop that may not pay
+ * cudaMalloc's implicit synchronisation, a binding that can pass only the
+ * operation's tensors).  No cudaMalloc, cudaFree or other allocating routine
+ * is called.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress, with that device current); make that first call
+ *    before any stream capture.
+ *  - num_splits/chunk_tokens = 0/0 plans automatically and reduces the split
+ *    count until the partials fit; explicit values, or a batch whose minimum
+ *    scratch exceeds the array, are rejected with LARA_ERR_RESULT_LEN and a
+ *    message naming the limit.
+ *  - Every call shares the one array: the status word and counters are zeroed
+ *    at the start of each call (stream-ordered), and calls that overlap on the
+ *    GPU (different streams, or concurrent host threads) race on it.
+ * No counterpart in the reference (the FPGA owns fixed on-chip buffers). */
+#define LARA_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+LARA_API int lara_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                     const int32_t* seq_lens, uint16_t* o, int batch, int n_q_heads,
+                                     int n_kv_heads, int head_dim, int max_seq_len, float scale, int num_splits,
+                                     int chunk_tokens, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Context API: the backing of the Python AttentionAccelerator.  The context */
 /* owns the HBM KV cache, device I/O buffers, a stream and timing events.   */

@@ -5,12 +5,22 @@
 * ``lara_b200.ops`` -- torch-tensor front end of the stateless kernels
   (decode, split-KV partials + LSE combine, KV append, bf16 pack, dense
   transaction, prefill).
-* ``lara_b200.parallel`` -- one process per GPU: batch/KV-head sharding and
-  split-KV across GPUs (NCCL all-gather of partials + LSE combine).
+* ``lara_b200.workloads`` -- seeded synthetic inputs of the benchmark configs.
+* ``lara_b200.build`` -- compiles liblara_b200.so in-tree with nvcc.
 
-Importing the package loads liblara_b200.so and fails if it is not built.
+The library is loaded by ``lara_b200._native`` (on first use of ``lib`` /
+``check`` here, or on import of any module that computes); a missing or
+stale library raises there -- there is no CPU fallback.
 """
 
-from ._native import LaraConfigError, LaraError, LaraTimeout, check, lib  # noqa: F401
+_NATIVE = ("lib", "check", "LaraError", "LaraConfigError", "LaraTimeout")
 
-__all__ = ["LaraConfigError", "LaraError", "LaraTimeout", "check", "lib"]
+__all__ = list(_NATIVE)
+
+
+def __getattr__(name):
+    if name in _NATIVE:
+        from . import _native
+
+        return getattr(_native, name)
+    raise AttributeError(f"module 'lara_b200' has no attribute {name!r}")

@@ -218,6 +218,13 @@ std::string describe_status(int bits) {
 
 }  // namespace
 
+namespace lara {
+int set_last_error(int code, const std::string& message) {
+  g_last_error = message;
+  return code;
+}
+}  // namespace lara
+
 // ===========================================================================
 // stateless API
 // ===========================================================================

@@ -4,6 +4,8 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
+
 #include <cuda_runtime.h>
 
 namespace lara {
@@ -85,5 +87,9 @@ cudaError_t kv_append_launch(uint16_t* k_cache, uint16_t* v_cache, int32_t* lens
 cudaError_t pack_bf16_launch(const float* src, uint16_t* dst, size_t n, cudaStream_t stream);
 
 int device_sm_count();
+
+// Record the calling thread's last error message (lara_last_error_string)
+// and return `code`.
+int set_last_error(int code, const std::string& message);
 
 }  // namespace lara
