@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2,
+                    help="BASELINE config (2 = the headline Llama-3-8B decode)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per rank (default: config 2's 64)")
     ap.add_argument("--seq-len", type=int, default=None)
     ap.add_argument("--splits", type=int, default=0, help="force the split count (0 = planner)")
@@ -269,24 +271,81 @@ def run_reference(args, rank: int, world: int) -> int:
     return 0
 
 
+def _setup_decode(args, cfg, rank, world, dev):
+    """Inputs, step function and per-rank bytes for configs 2/3/4.
+
+    Config 2: each rank runs its own batch (weak scaling).  Config 3: the 256
+    ragged sequences are partitioned across ranks by token count (strong).
+    Config 4: every sequence's tokens are split across ranks (split-KV,
+    strong); the step is partial decode + NCCL all-gather + LSE combine."""
+    import torch
+
+    from lara_b200 import ops, parallel
+    from lara_b200.workloads import make_decode_inputs
+
+    info = {}
+    if cfg.name == "llama3_8b_decode":
+        B = args.batch or cfg.batch
+        L = args.seq_len or cfg.seq_len
+        q, k, v, lens = make_decode_inputs(cfg, dev, batch=B, seq_len=L, seed=cfg.seed + 1000 * rank)
+        scaling, global_batch = "weak", B * world
+    elif cfg.name == "ragged_decode_stress":
+        all_lens = cfg.lens()
+        mine = parallel.balanced_partition(all_lens, world)[rank] if world > 1 else list(range(cfg.batch))
+        L = int(all_lens[mine].max())
+        q, k, v, lens = make_decode_inputs(cfg, dev, lens=all_lens[mine], capacity=L, seed=cfg.seed + 1000 * rank)
+        B = len(mine)
+        scaling, global_batch = "strong", cfg.batch
+        info["sequences_on_rank0"] = len(mine)
+    else:  # long-context split-KV
+        B = args.batch or cfg.batch
+        L_total = args.seq_len or cfg.seq_len
+        start, L = parallel.token_range(L_total, world, rank)
+        # every rank draws its own token slice (seeded by rank); q is shared
+        q, k, v, lens = make_decode_inputs(cfg, dev, batch=B, seq_len=L, seed=cfg.seed + 1000 * rank)
+        g = torch.Generator(device=dev)
+        g.manual_seed(cfg.seed)
+        q = (torch.randn(q.shape, generator=g, device=dev) * cfg.std).to(torch.bfloat16)
+        scaling, global_batch = "strong", B
+        info["tokens_per_rank"] = L
+    lens_np = lens.cpu().numpy()
+    nbytes = cfg.kv_bytes(lens_np)
+    o = torch.empty_like(q)
+    if cfg.name == "long_context_splitkv" and world > 1:
+        dec = parallel.SplitKVDecoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, L, dev, lens_local=lens_np)
+        plan = dec.decoder.plan
+
+        def step():
+            dec(q, k, v, lens, out=o)
+        launches = 3  # partial decode, NCCL all-gather, combine
+    else:
+        dec = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, L, dev, lens=lens_np,
+                          num_splits=args.splits, chunk_tokens=args.chunk)
+        plan = dec.plan
+
+        def step():
+            dec(q, k, v, lens, out=o)
+        launches = 1
+    info.update({"splits": plan.num_splits, "chunk_tokens": plan.chunk_tokens})
+    ws = dec.decoder.workspace if hasattr(dec, "decoder") else dec.workspace
+    return dict(q=q, k=k, v=v, lens=lens, lens_np=lens_np, o=o, B=B, L=L, nbytes=nbytes, step=step, ws=ws,
+                scaling=scaling, global_batch=global_batch, info=info, launches=launches)
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     import torch
     import torch.distributed as dist
 
     from lara_b200 import ops
-    from lara_b200.workloads import CONFIGS, make_decode_inputs
+    from lara_b200.workloads import CONFIGS
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    cfg = CONFIGS[2]
-    B = args.batch or cfg.batch
-    L = args.seq_len or cfg.seq_len
-    q, k, v, lens = make_decode_inputs(cfg, dev, batch=B, seq_len=L, seed=cfg.seed + 1000 * rank)
-    lens_np = lens.cpu().numpy()
-    nbytes = cfg.kv_bytes(lens_np)
-    dec = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, L, dev, lens=lens_np,
-                      num_splits=args.splits, chunk_tokens=args.chunk)
-    o = torch.empty_like(q)
+    cfg = CONFIGS[args.config]
+    S = _setup_decode(args, cfg, rank, world, dev)
+    q, k, v, lens, lens_np, o, B, L, nbytes = (S[x] for x in ("q", "k", "v", "lens", "lens_np", "o", "B", "L",
+                                                              "nbytes"))
+    step = S["step"]
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -294,9 +353,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
             dist.barrier(device_ids=[local_rank])
 
     for _ in range(args.warmup):
-        dec(q, k, v, lens, out=o)
+        step()
     torch.cuda.synchronize(dev)
-    if ops.workspace_status(dec.workspace) != 0:
+    if ops.workspace_status(S["ws"]) != 0:
         raise RuntimeError("decode kernel reported a device error status during warm-up")
 
     uuid = None
@@ -311,77 +370,112 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     sampler.start()
     ev0.record(stream)
     for _ in range(args.steps):
-        dec(q, k, v, lens, out=o)
+        step()
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     sampler.stop()
     barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
     clocks = sampler.summary()
-    if ops.workspace_status(dec.workspace) != 0:
+    if ops.workspace_status(S["ws"]) != 0:
         raise RuntimeError("decode kernel reported a device error status")
 
     # e2e through the public API with pinned host buffers
     e2e_ms = None
     h2d = d2h = 0
+    e2e_api = None
     if not args.no_e2e:
-        import ctypes
+        q_host = q.view(torch.int16).cpu().pin_memory()
+        o_host = torch.empty_like(q_host).pin_memory()
+        qn = q_host.numpy().view(np.uint16)
+        on = o_host.numpy().view(np.uint16)
+        e2e_steps = max(10, args.steps // 4)
+        if world == 1 or cfg.name != "long_context_splitkv":
+            import ctypes
 
-        from lara_b200 import _native
-        from lara_b200.attn_driver import AttentionAccelerator
+            from lara_b200 import _native
+            from lara_b200.attn_driver import AttentionAccelerator
 
-        with AttentionAccelerator(device=local_rank) as acc:
-            acc.configure_heads(cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, max_seq_len=L, batch=B)
-            # device-resident cache load through the C ABI (on_device = 1)
-            _native.check(_native.lib.lara_kv_load(acc._ctx, k.data_ptr(), v.data_ptr(),
-                                                   lens_np.ctypes.data_as(ctypes.c_void_p), L, 1), "kv_load")
-            q_host = q.view(torch.int16).cpu().pin_memory()
-            o_host = torch.empty_like(q_host).pin_memory()
-            qn = q_host.numpy().view(np.uint16)
-            on = o_host.numpy().view(np.uint16)
-            for _ in range(max(3, min(args.warmup, 20))):
-                acc.run_query(qn, out=on)
-            e2e_steps = max(10, args.steps // 4)
+            with AttentionAccelerator(device=local_rank) as acc:
+                acc.configure_heads(cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, max_seq_len=L, batch=B)
+                # device-resident cache load through the C ABI (on_device = 1)
+                _native.check(_native.lib.lara_kv_load(acc._ctx, k.data_ptr(), v.data_ptr(),
+                                                       lens_np.ctypes.data_as(ctypes.c_void_p), L, 1), "kv_load")
+                for _ in range(max(3, min(args.warmup, 20))):
+                    acc.run_query(qn, out=on)
+                barrier()
+                t0 = time.perf_counter()
+                for _ in range(e2e_steps):
+                    acc.run_query(qn, out=on)
+                e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+                barrier()
+            e2e_api = "AttentionAccelerator.run_query (pinned host q/o)"
+        else:
+            qd, od = q.view(torch.int16), o.view(torch.int16)
+
+            def e2e_step():
+                qd.copy_(q_host, non_blocking=True)
+                step()
+                o_host.copy_(od, non_blocking=True)
+                torch.cuda.synchronize(dev)
+            for _ in range(3):
+                e2e_step()
             barrier()
             t0 = time.perf_counter()
             for _ in range(e2e_steps):
-                acc.run_query(qn, out=on)
+                e2e_step()
             e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
             barrier()
-            h2d, d2h = qn.nbytes, on.nbytes
-            # the API result equals the stateless kernel's
-            if not np.array_equal(on, o.view(torch.int16).cpu().numpy().view(np.uint16)):
-                raise RuntimeError("run_query output differs from the kernel output")
+            e2e_api = "lara_b200.parallel.SplitKVDecoder with pinned host q/o copies"
+        h2d, d2h = qn.nbytes, on.nbytes
+        if not np.array_equal(on, o.view(torch.int16).cpu().numpy().view(np.uint16)):
+            raise RuntimeError("API output differs from the timed kernel output")
 
-    # max over ranks
+    # max over ranks; bytes summed over ranks
+    total_bytes = nbytes
     if world > 1:
         t = torch.tensor([ms, e2e_ms or 0.0], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms = float(t[0]), (float(t[1]) if e2e_ms is not None else None)
+        nb = torch.tensor([nbytes], dtype=torch.float64, device=dev)
+        dist.all_reduce(nb, op=dist.ReduceOp.SUM)
+        total_bytes = int(nb.item())
 
     if rank != 0:
         return 0
     peak, peak_kind = measured_peak()
-    value = nbytes * world / (ms * 1e-3) / 1e9
-    achieved = nbytes / (ms * 1e-3) / 1e9  # one launch per step on each GPU
-    traffic = profiled_traffic()
+    value = total_bytes / (ms * 1e-3) / 1e9
+    achieved = nbytes / (ms * 1e-3) / 1e9  # this GPU's bytes over the step
+    traffic = profiled_traffic() if cfg.name == "llama3_8b_decode" else None
     cpu = None
     if not args.no_cpu_baseline and world == 1:
-        qn_, kn_, vn_ = (t.view(torch.int16).cpu().numpy().view(np.uint16) for t in (q, k, v))
         cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-        gbs, steps_done, el = cpu_decode_rate(qn_, kn_, vn_, lens_np, args.cpu_seconds, cores)
+        # bounded sample: as many whole sequences as fit ~4 GB of bf16 on the host
+        per_seq = [int(x) * cfg.n_kv_heads * cfg.head_dim * 4 for x in lens_np]
+        nseq, acc_b = 0, 0
+        while nseq < B and (nseq == 0 or acc_b + per_seq[nseq] <= 4 << 30):
+            acc_b += per_seq[nseq]
+            nseq += 1
+        Ls = int(lens_np[:nseq].max())
+        qn_, kn_, vn_ = (t[:nseq, :, :Ls].contiguous() if t.dim() == 4 else t[:nseq].contiguous()
+                         for t in (q, k, v))
+        qn_, kn_, vn_ = (t.view(torch.int16).cpu().numpy().view(np.uint16) for t in (qn_, kn_, vn_))
+        gbs, steps_done, el = cpu_decode_rate(qn_, kn_, vn_, lens_np[:nseq], args.cpu_seconds, cores)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-               "sample": f"{steps_done} full decode step(s) of this workload ({B} seqs x {L} tokens) in "
-                         f"{el:.1f} s, oracle restatement of sw/board_performance.py:158-192, {cores} threads"}
+               "sample": f"{steps_done} pass(es) over {nseq} of {B} sequences ({int(lens_np[:nseq].sum())} tokens) "
+                         f"in {el:.1f} s; oracle restatement of sw/board_performance.py:158-192, {cores} threads"}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": S["scaling"],
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": cfg.name, "global_batch": B * world, "batch_per_gpu": B, "seq_len": L,
+        "config": {"workload": cfg.name, "global_batch": S["global_batch"], "batch_per_gpu": B, "seq_len": L,
                    "n_q_heads": cfg.n_q_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
-                   "parallelism": f"batch-sharded x{world}", "l2": "inputs (1 GiB/GPU) larger than L2, no flush",
-                   "splits": dec.plan.num_splits, "chunk_tokens": dec.plan.chunk_tokens},
-        "queries_per_s": round(B * world / (ms * 1e-3), 1),
+                   "parallelism": {"llama3_8b_decode": f"batch-sharded x{world}",
+                                   "ragged_decode_stress": f"token-balanced batch partition x{world}",
+                                   "long_context_splitkv": f"split-KV x{world} (NCCL all-gather + LSE combine)"
+                                   }[cfg.name],
+                   "l2": "inputs larger than L2, no flush", **S["info"]},
+        "queries_per_s": round(S["global_batch"] / (ms * 1e-3), 1),
         "pct_hbm_peak": round(100.0 * achieved / peak, 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -389,10 +483,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
                      else "fallback 6650 GB/s", "algorithmic_bytes_per_launch": nbytes},
         "cpu_baseline": cpu,
         "e2e": None if e2e_ms is None else {
-            "value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
-            "api": "AttentionAccelerator.run_query (pinned host q/o)"},
-        "gpu_launches": args.steps,
+            "api": e2e_api},
+        "gpu_launches": args.steps * S["launches"],
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

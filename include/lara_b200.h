@@ -112,6 +112,15 @@ LARA_API int lara_gqa_decode_partial(const uint16_t* q, const uint16_t* k_cache,
 LARA_API int lara_lse_combine(const float* part_ml, const float* part_acc, int num_parts, int rows, int head_dim,
                      uint16_t* o, void* stream);
 
+/* lara_lse_combine with explicit per-part strides (in floats): part i's (m, l)
+ * pairs start at part_ml + i*ml_part_stride and its acc rows at
+ * part_acc + i*acc_part_stride.  Lets each device keep its partial state
+ * packed as [rows*2 (m,l) | rows*D acc] so one all-gather moves it.
+ * Replaces: as lara_lse_combine (hw/rtl/mem/output_buffer.sv:271-286). */
+LARA_API int lara_lse_combine_strided(const float* part_ml, long long ml_part_stride, const float* part_acc,
+                                      long long acc_part_stride, int num_parts, int rows, int head_dim, uint16_t* o,
+                                      void* stream);
+
 /* Append n_new tokens per sequence: k_new/v_new[B][Hkv][n_new][D] are written
  * at positions seq_lens[b] .. seq_lens[b]+n_new-1 of the cache, then
  * seq_lens[b] += n_new.  Rows that would pass max_seq_len are dropped and

@@ -73,6 +73,8 @@ SIGNATURES = {
     "lara_gqa_decode_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                         c_int, c_int, c_float, c_int, c_int, c_void_p]),
     "lara_lse_combine": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "lara_lse_combine_strided": (c_int, [c_void_p, ctypes.c_longlong, c_void_p, ctypes.c_longlong, c_int, c_int,
+                                         c_int, c_void_p, c_void_p]),
     "lara_kv_append": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                c_void_p, c_void_p]),
     "lara_pack_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -306,8 +306,25 @@ int lara_lse_combine(const float* part_ml, const float* part_acc, int num_parts,
   if (num_parts < 1 || rows < 1 || head_dim < 2 || head_dim % 2)
     return fail(LARA_ERR_BAD_CFG, "num_parts, rows must be >= 1 and head_dim even");
   if (!aligned(part_acc, 8) || !aligned(o, 4)) return fail(LARA_ERR_STREAM_DEST, "misaligned buffer");
-  cudaError_t e = lara::lse_combine_launch(part_ml, part_acc, num_parts, rows, rows, head_dim, o, nullptr, nullptr,
-                                           static_cast<cudaStream_t>(stream));
+  cudaError_t e = lara::lse_combine_launch(part_ml, 2LL * rows, part_acc, (long long)rows * head_dim, num_parts, rows,
+                                           head_dim, o, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lse_combine launch");
+  return LARA_OK;
+}
+
+int lara_lse_combine_strided(const float* part_ml, long long ml_part_stride, const float* part_acc,
+                             long long acc_part_stride, int num_parts, int rows, int head_dim, uint16_t* o,
+                             void* stream) {
+  if (!part_ml || !part_acc || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
+  if (num_parts < 1 || rows < 1 || head_dim < 2 || head_dim % 2)
+    return fail(LARA_ERR_BAD_CFG, "num_parts, rows must be >= 1 and head_dim even");
+  if (ml_part_stride < 2LL * rows || acc_part_stride < (long long)rows * head_dim || ml_part_stride % 2 ||
+      acc_part_stride % 2)
+    return fail(LARA_ERR_BAD_CFG, "part strides must be even and cover rows*2 / rows*head_dim floats");
+  if (!aligned(part_ml, 8) || !aligned(part_acc, 8) || !aligned(o, 4))
+    return fail(LARA_ERR_STREAM_DEST, "misaligned buffer");
+  cudaError_t e = lara::lse_combine_launch(part_ml, ml_part_stride, part_acc, acc_part_stride, num_parts, rows,
+                                           head_dim, o, nullptr, nullptr, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lse_combine launch");
   return LARA_OK;
 }

@@ -542,11 +542,11 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
       const long long ctas = (long long)batch * n_kv_heads * ((len0 + chunk - 1) / chunk);
       const long long per_sm = (ctas + sms - 1) / sms;
       const int per = len0 < chunk ? len0 : chunk;
-      // The busiest SM runs its CTAs `cps` at a time; a CTA left running
-      // alone streams at about 70% of the SM's two-CTA rate (measured on
-      // B200 in config-2 split sweeps).
-      const long long alone = cps > 1 ? per_sm % cps : 0;
-      cost = (double)(per_sm - alone) * (per + ovh) + (double)alone * (per + ovh) / 0.7;
+      // An SM that only ever holds one CTA streams at about 70% of the rate
+      // it reaches with two resident CTAs (config-2 split sweeps on B200);
+      // with more CTAs per SM the neighbour hides each one's prologue.
+      const double lone = (cps > 1 && per_sm == 1) ? 1.0 / 0.7 : 1.0;
+      cost = (double)per_sm * (per + ovh) * lone;
     } else {
       long long ctas = 0;
       for (int b = 0; b < batch; ++b) ctas += (lens_host[b] + chunk - 1) / chunk;

@@ -67,29 +67,32 @@ __global__ void pack_bf16_kernel(const float* __restrict__ src, uint16_t* __rest
     for (size_t i = nvec * 4; i < n; ++i) dst[i] = (uint16_t)f32_to_bf16_rne_bits(src[i]);
 }
 
-// One warp per output row; lanes stride over the head dims.
-__global__ void lse_combine_kernel(const float* __restrict__ part_ml, const float* __restrict__ part_acc,
-                                   int num_parts, long long stride_rows, int rows, int head_dim,
-                                   uint16_t* __restrict__ o, float* __restrict__ out_ml,
+// One warp per output row; lanes stride over the head dims.  Part i of row r
+// has (m, l) at part_ml[i * ml_stride + r * 2] and acc at
+// part_acc[i * acc_stride + r * head_dim] (strides in floats), so partials
+// gathered from several devices can stay packed per device.
+__global__ void lse_combine_kernel(const float* __restrict__ part_ml, long long ml_stride,
+                                   const float* __restrict__ part_acc, long long acc_stride, int num_parts,
+                                   int rows, int head_dim, uint16_t* __restrict__ o, float* __restrict__ out_ml,
                                    float* __restrict__ out_acc) {
   const int warps_per_block = blockDim.x / 32;
   const int row = blockIdx.x * warps_per_block + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float M = -INFINITY;
-  for (int i = 0; i < num_parts; ++i) M = fmaxf(M, part_ml[(i * stride_rows + row) * 2]);
+  for (int i = 0; i < num_parts; ++i) M = fmaxf(M, part_ml[i * ml_stride + row * 2]);
   const float Mu = (M == -INFINITY) ? 0.f : M;
   float L = 0.f;
   for (int i = 0; i < num_parts; ++i) {
-    const float* ml = part_ml + (i * stride_rows + row) * 2;
+    const float* ml = part_ml + i * ml_stride + row * 2;
     L = fmaf(ml[1], exp2f(ml[0] - Mu), L);
   }
   const float inv = (L > 0.f) ? 1.f / L : 0.f;
   for (int d = lane * 2; d < head_dim; d += 64) {
     float o0 = 0.f, o1 = 0.f;
     for (int i = 0; i < num_parts; ++i) {
-      const float sc = exp2f(part_ml[(i * stride_rows + row) * 2] - Mu);
-      const float2 a = *reinterpret_cast<const float2*>(part_acc + (i * stride_rows + row) * head_dim + d);
+      const float sc = exp2f(part_ml[i * ml_stride + row * 2] - Mu);
+      const float2 a = *reinterpret_cast<const float2*>(part_acc + i * acc_stride + (long long)row * head_dim + d);
       o0 = fmaf(a.x, sc, o0);
       o1 = fmaf(a.y, sc, o1);
     }
@@ -133,13 +136,13 @@ cudaError_t pack_bf16_launch(const float* src, uint16_t* dst, size_t n, cudaStre
   return cudaGetLastError();
 }
 
-cudaError_t lse_combine_launch(const float* part_ml, const float* part_acc, int num_parts, long long part_stride_rows,
-                               int rows, int head_dim, uint16_t* o, float* out_ml, float* out_acc,
+cudaError_t lse_combine_launch(const float* part_ml, long long ml_stride, const float* part_acc, long long acc_stride,
+                               int num_parts, int rows, int head_dim, uint16_t* o, float* out_ml, float* out_acc,
                                cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const int warps = 8;
   lse_combine_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, stream>>>(
-      part_ml, part_acc, num_parts, part_stride_rows, rows, head_dim, o, out_ml, out_acc);
+      part_ml, ml_stride, part_acc, acc_stride, num_parts, rows, head_dim, o, out_ml, out_acc);
   return cudaGetLastError();
 }
 

@@ -76,8 +76,11 @@ int decode_tile_tokens(int head_dim, int group);
 
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream);
 
-cudaError_t lse_combine_launch(const float* part_ml, const float* part_acc, int num_parts, long long part_stride_rows,
-                               int rows, int head_dim, uint16_t* o, float* out_ml, float* out_acc,
+// Merge `num_parts` partial states of `rows` rows; part i's (m, l) pairs start
+// at part_ml + i * ml_stride, its acc rows at part_acc + i * acc_stride
+// (floats).  Writes bf16 `o` if non-null, else the merged (m, l, acc).
+cudaError_t lse_combine_launch(const float* part_ml, long long ml_stride, const float* part_acc, long long acc_stride,
+                               int num_parts, int rows, int head_dim, uint16_t* o, float* out_ml, float* out_acc,
                                cudaStream_t stream);
 
 cudaError_t kv_append_launch(uint16_t* k_cache, uint16_t* v_cache, int32_t* lens, const uint16_t* k_new,

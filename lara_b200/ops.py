@@ -139,6 +139,25 @@ def lse_combine(part_ml: torch.Tensor, part_acc: torch.Tensor) -> torch.Tensor:
     return o
 
 
+def lse_combine_strided(buf: torch.Tensor, num_parts: int, rows: int, head_dim: int, *, ml_offset: int,
+                        acc_offset: int, part_stride: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge partial states packed in one float32 buffer: part i's (m, l) pairs
+    at ``buf[i*part_stride + ml_offset:]``, its acc rows at
+    ``buf[i*part_stride + acc_offset:]``.  Returns bf16 ``[rows, head_dim]``
+    (or writes ``out``)."""
+    if buf.dtype != torch.float32 or not buf.is_contiguous():
+        raise ValueError("buf must be a contiguous float32 tensor")
+    need = (num_parts - 1) * part_stride + max(ml_offset + 2 * rows, acc_offset + rows * head_dim)
+    if buf.numel() < need:
+        raise ValueError(f"buf holds {buf.numel()} floats, {need} needed")
+    o = torch.empty((rows, head_dim), dtype=torch.bfloat16, device=buf.device) if out is None else out
+    base = buf.data_ptr()
+    check(lib.lara_lse_combine_strided(base + 4 * ml_offset, part_stride, base + 4 * acc_offset, part_stride,
+                                       num_parts, rows, head_dim, o.data_ptr(), _stream(buf.device)),
+          "lara_lse_combine_strided")
+    return o
+
+
 def kv_append(k_cache, v_cache, seq_lens, k_new, v_new, workspace=None) -> None:
     """Write ``k_new/v_new[B, Hkv, n, D]`` at ``seq_lens[b]`` and advance ``seq_lens``."""
     B, Hkv, Lmax, D = k_cache.shape
@@ -170,7 +189,7 @@ def attention_dense(q, k, v, *, causal=True, q_pos_base=0, kv_pos_base=0, scale=
     sc = 1.0 / math.sqrt(D) if scale is None else float(scale)
     nbytes = int(lib.lara_dense_workspace_bytes(Hq, Hkv, D, L))
     if nbytes == 0:
-        check(0x01 if L >= 1 else 0x01, "lara_dense_workspace_bytes")
+        raise ValueError(f"unsupported dense geometry Hq={Hq} Hkv={Hkv} D={D} L={L}")
     ws = new_workspace(nbytes, q.device)
     o = torch.empty_like(q)
     check(lib.lara_attention_dense(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), Hq, Hkv, D, L,

@@ -88,18 +88,23 @@ PREFILL = PrefillConfig()
 
 
 def make_decode_inputs(cfg: DecodeConfig, device, *, batch: int | None = None, seq_len: int | None = None,
-                       seed: int | None = None, capacity: int | None = None):
+                       seed: int | None = None, capacity: int | None = None, lens=None):
     """Device tensors (q, k_cache, v_cache, lens) for a decode config.
 
-    ``batch``/``seq_len`` shrink the workload (tests); ``capacity`` is the
-    cache's token capacity (default: the longest sequence).
+    ``batch``/``seq_len`` shrink the workload (tests); ``lens`` gives explicit
+    per-sequence lengths (a rank's share of a ragged batch); ``capacity`` is
+    the cache's token capacity (default: the longest sequence).
     """
     import torch
 
-    B = cfg.batch if batch is None else batch
-    lens = cfg.lens(B) if seq_len is None else np.full(B, seq_len, np.int32)
-    if seq_len is not None and cfg.ragged:
-        lens = np.minimum(cfg.lens(B), seq_len).astype(np.int32)
+    if lens is not None:
+        lens = np.asarray(lens, dtype=np.int32)
+        B = len(lens)
+    else:
+        B = cfg.batch if batch is None else batch
+        lens = cfg.lens(B) if seq_len is None else np.full(B, seq_len, np.int32)
+        if seq_len is not None and cfg.ragged:
+            lens = np.minimum(cfg.lens(B), seq_len).astype(np.int32)
     cap = int(lens.max()) if capacity is None else int(capacity)
     dev = torch.device(device)
     g = torch.Generator(device=dev)

@@ -21,6 +21,8 @@ from .attention import (  # noqa: F401
     cpu_attention_numpy,
     decode_attention,
     decode_attention_fp64,
+    decode_partial,
+    lse_combine,
     fp32_to_bf16_u16,
     numeric_error,
     prefill_attention,
