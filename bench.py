@@ -61,8 +61,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2,
-                    help="BASELINE config (2 = the headline Llama-3-8B decode)")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
+                    help="BASELINE config (2 = the headline Llama-3-8B decode; 5 = chunked prefill)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per rank (default: config 2's 64)")
     ap.add_argument("--seq-len", type=int, default=None)
     ap.add_argument("--splits", type=int, default=0, help="force the split count (0 = planner)")
@@ -493,6 +493,116 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
+    """Config 5: chunked prefill on the tensor cores (TFLOP/s).
+
+    One step = append the 2048 new K/V tokens of every sequence at position
+    8192 (lengths reset first) + causal attention of the 2048 new queries over
+    cache + self.  Sequences are split across ranks (weak scaling: each rank
+    runs config 5's 4 sequences)."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from lara_b200 import _native, ops
+    from lara_b200.workloads import PREFILL, make_prefill_inputs
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = PREFILL
+    q, k, v, kn, vn, lens0 = make_prefill_inputs(cfg, dev)
+    B, n, C = cfg.batch, cfg.new, cfg.cached
+    Lmax = C + n
+    lens = lens0.clone()
+    nb = int(_native.lib.lara_prefill_workspace_bytes(B, n, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, Lmax))
+    ws = ops.new_workspace(nb, dev)
+    o = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+    scale = 1.0 / (cfg.head_dim ** 0.5)
+
+    def step():
+        lens.copy_(lens0)
+        ops.kv_append(k, v, lens, kn, vn, workspace=ws)
+        _native.check(_native.lib.lara_gqa_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), lens0.data_ptr(),
+                                                   o.data_ptr(), B, n, cfg.n_q_heads, cfg.n_kv_heads,
+                                                   cfg.head_dim, Lmax, 1, scale, ws.data_ptr(), ws.numel(),
+                                                   stream.cuda_stream), "prefill")
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if ops.workspace_status(ws) != 0:
+        raise RuntimeError("prefill reported a device error status")
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.start()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    sampler.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    # kernel-only time of the attention launch (for the roofline)
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lens.copy_(lens0)
+    ka.record(stream)
+    for _ in range(max(3, args.steps // 4)):
+        _native.check(_native.lib.lara_gqa_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), lens0.data_ptr(),
+                                                   o.data_ptr(), B, n, cfg.n_q_heads, cfg.n_kv_heads,
+                                                   cfg.head_dim, Lmax, 1, scale, ws.data_ptr(), ws.numel(),
+                                                   stream.cuda_stream), "prefill")
+    kb.record(stream)
+    torch.cuda.synchronize(dev)
+    k_ms = ka.elapsed_time(kb) / max(3, args.steps // 4)
+    clocks = sampler.summary()
+    if world > 1:
+        t = torch.tensor([ms, k_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, k_ms = float(t[0]), float(t[1])
+    if rank != 0:
+        return 0
+    flops = cfg.flops()
+    peak = 1415.2
+    peak_src = "fallback 1400 TFLOP/s sustained"
+    pp = ROOT / "MEASURED_PEAKS.json"
+    if pp.exists():
+        try:
+            peak = float(json.loads(pp.read_text())["bf16_tflops_sustained"])
+            peak_src = "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+        except (ValueError, KeyError):
+            pass
+    achieved = flops / (k_ms * 1e-3) / 1e12
+    line = {
+        "metric": "chunked-prefill attention TFLOP/s (tensor-core path)", "value": round(flops * world / (ms * 1e-3) / 1e12, 2),
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "batch_per_gpu": B, "new_tokens": n, "cached_tokens": C,
+                   "n_q_heads": cfg.n_q_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
+                   "causal": True, "step": "length reset + K/V append + attention",
+                   "split_p": os.environ.get("LARA_TC_SPLIT_P", "1") != "0"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                     "algorithmic_flop_per_launch": flops, "attention_kernel_ms": round(k_ms, 4)},
+        "gpu_launches": args.steps * 3, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main() -> int:
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -512,6 +622,8 @@ def main() -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.config == 5:
+            return run_prefill(args, rank, world, local_rank)
         return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1 and dist.is_initialized():

@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -119,6 +120,43 @@ int decode_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, const
   return LARA_OK;
 }
 
+// Which kernel runs prefill / dense attention: the tcgen05 tensor-core
+// kernel for head_dim 128 (default), or the CUDA-core streaming kernel.
+// LARA_ATTN_PATH=stream|tc overrides (tc fails if the geometry has no
+// tensor-core kernel).
+enum class AttnPath { kAuto, kStream, kTensor };
+
+AttnPath attn_path_override() {
+  const char* e = std::getenv("LARA_ATTN_PATH");
+  if (!e) return AttnPath::kAuto;
+  if (std::strcmp(e, "stream") == 0) return AttnPath::kStream;
+  if (std::strcmp(e, "tc") == 0) return AttnPath::kTensor;
+  return AttnPath::kAuto;
+}
+
+// Launch the tensor-core kernel if selected; returns LARA_OK when it ran,
+// -1 when the streaming kernel should run instead, or an error code.
+int try_tensor_path(lara::PrefillTcParams tp, cudaStream_t st) {
+  const AttnPath path = attn_path_override();
+  // LARA_TC_SPLIT_P=0 rounds P to one bf16 (faster, ~1 bf16 ulp of the row
+  // scale); the default splits P into two bf16 terms.
+  const char* sp = std::getenv("LARA_TC_SPLIT_P");
+  tp.split_p = (sp && std::strcmp(sp, "0") == 0) ? 0 : 1;
+  if (path == AttnPath::kStream) return -1;
+  if (!lara::prefill_tc_supported(tp.head_dim, tp.n_q_heads, tp.n_kv_heads)) {
+    if (path == AttnPath::kTensor)
+      return fail(LARA_ERR_UNSUPPORTED, "LARA_ATTN_PATH=tc but no tensor-core kernel for head_dim=%d", tp.head_dim);
+    return -1;
+  }
+  const cudaError_t e = lara::prefill_tc_launch(tp, st);
+  if (e == cudaSuccess) return LARA_OK;
+  if (e == cudaErrorInvalidValue && path != AttnPath::kTensor) {
+    cudaGetLastError();  // tensor map not encodable for this shape: stream instead
+    return -1;
+  }
+  return cuda_fail(e, "tensor-core attention launch");
+}
+
 size_t dense_ws_bytes(int hq, int hkv, int d, int L, int* nsplit, int* chunk) {
   lara::decode_plan(L, hkv, hq, d, L, nullptr, nsplit, chunk);
   return lara::decode_workspace_layout(L, hq, hkv, d, *nsplit).total;
@@ -131,6 +169,18 @@ int dense_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16
   if (!q || !k || !v || !o || !ws) return fail(LARA_ERR_STREAM_DEST, "null tensor or workspace pointer");
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 4) || !aligned(ws, 256))
     return fail(LARA_ERR_STREAM_DEST, "q/k/v must be 16-byte aligned, o 4-byte, workspace 256-byte");
+  {
+    lara::PrefillTcParams tp{};
+    tp.q = q; tp.q_sb = (long long)hq * L * d; tp.q_sr = d; tp.q_sh = (long long)L * d;
+    tp.k = k; tp.v = v; tp.kv_rows = L;
+    tp.o = o; tp.o_sb = tp.q_sb; tp.o_sr = d; tp.o_sh = (long long)L * d;
+    tp.batch = 1; tp.n_q = L; tp.n_q_heads = hq; tp.n_kv_heads = hkv; tp.head_dim = d;
+    tp.base_lens = nullptr; tp.kv_add = L; tp.q_add = q_pos_base - kv_pos_base; tp.causal = causal ? 1 : 0;
+    tp.scale_log2 = scale * 1.4426950408889634f;
+    tp.status = static_cast<int*>(ws);
+    const int r = try_tensor_path(tp, static_cast<cudaStream_t>(stream));
+    if (r != -1) return r;
+  }
   int nsplit = 0, chunk = 0;
   const size_t need = dense_ws_bytes(hq, hkv, d, L, &nsplit, &chunk);
   if (ws_bytes < need) return fail(LARA_ERR_RESULT_LEN, "workspace has %zu bytes, %zu needed", ws_bytes, need);
@@ -182,6 +232,18 @@ int prefill_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 4) || !aligned(ws, 256))
     return fail(LARA_ERR_STREAM_DEST, "q/k/v must be 16-byte aligned, o 4-byte, workspace 256-byte");
   if (!(scale > 0.f) || !std::isfinite(scale)) return fail(LARA_ERR_BAD_CFG, "scale must be positive and finite");
+  {
+    lara::PrefillTcParams tp{};
+    tp.q = q; tp.q_sb = (long long)n_new * hq * d; tp.q_sr = (long long)hq * d; tp.q_sh = d;
+    tp.k = k; tp.v = v; tp.kv_rows = lmax;
+    tp.o = o; tp.o_sb = tp.q_sb; tp.o_sr = tp.q_sr; tp.o_sh = d;
+    tp.batch = batch; tp.n_q = n_new; tp.n_q_heads = hq; tp.n_kv_heads = hkv; tp.head_dim = d;
+    tp.base_lens = cached_lens; tp.kv_add = n_new; tp.q_add = 0; tp.causal = causal ? 1 : 0;
+    tp.scale_log2 = scale * 1.4426950408889634f;
+    tp.status = static_cast<int*>(ws);
+    const int r = try_tensor_path(tp, static_cast<cudaStream_t>(stream));
+    if (r != -1) return r;
+  }
   int nsplit = 0, chunk = 0;
   const size_t need = prefill_ws_bytes(batch, n_new, hq, hkv, d, lmax, &nsplit, &chunk);
   if (ws_bytes < need) return fail(LARA_ERR_RESULT_LEN, "workspace has %zu bytes, %zu needed", ws_bytes, need);

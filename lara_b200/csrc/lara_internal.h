@@ -76,6 +76,30 @@ int decode_tile_tokens(int head_dim, int group);
 
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream);
 
+// Tensor-core (tcgen05/TMEM) attention of n_q query rows per sequence over a
+// bf16 KV cache [batch][Hkv][kv_rows][128].  Sequence b has
+// kv_len = base + kv_add keys (base = base_lens[b] or 0) and query row i sees
+// keys j <= base + q_add + i when causal.
+struct PrefillTcParams {
+  const uint16_t* q;           // q[b * q_sb + i * q_sr + h * q_sh + d]
+  long long q_sb, q_sr, q_sh;
+  const uint16_t* k;
+  const uint16_t* v;
+  int kv_rows;
+  uint16_t* o;                 // same indexing as q with o_* strides
+  long long o_sb, o_sr, o_sh;
+  int batch, n_q, n_q_heads, n_kv_heads, head_dim;
+  const int32_t* base_lens;
+  int kv_add, q_add;
+  int causal;
+  float scale_log2;
+  int* status;
+  int split_p;                 // 1: P = P_hi + P_lo (two bf16 MMA passes); 0: P in one bf16
+};
+
+bool prefill_tc_supported(int head_dim, int n_q_heads, int n_kv_heads);
+cudaError_t prefill_tc_launch(const PrefillTcParams& p, cudaStream_t stream);
+
 // Merge `num_parts` partial states of `rows` rows; part i's (m, l) pairs start
 // at part_ml + i * ml_stride, its acc rows at part_acc + i * acc_stride
 // (floats).  Writes bf16 `o` if non-null, else the merged (m, l, acc).

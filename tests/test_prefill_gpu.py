@@ -1,0 +1,121 @@
+"""GPU parity of chunked prefill ("cache + self") and of the tensor-core path.
+
+``lara_gqa_prefill`` runs the tcgen05/TMEM kernel for head_dim 128 and the
+CUDA-core streaming kernel otherwise; ``LARA_ATTN_PATH=tc|stream`` selects one
+explicitly, so both are checked against the CPU oracle (``prefill_attention``,
+the causal rule of ``sw/board_performance.py:174-177`` over cache + self).
+Tolerance as in ``tests/parity.py`` (<= 2 bf16 ulp, also vs fp64).  The
+tensor-core path rounds P to bf16 (round to nearest even) before P.V.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import oracle  # noqa: E402
+from parity import assert_bf16_parity, words_of  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _prefill(dev, q, k, v, cached, causal):
+    from lara_b200 import _native, ops
+
+    B, n, Hq, D = q.shape
+    _, Hkv, Lmax, _ = k.shape
+    lens = torch.tensor(cached, dtype=torch.int32, device=dev)
+    nbytes = int(_native.lib.lara_prefill_workspace_bytes(B, n, Hq, Hkv, D, Lmax))
+    ws = ops.new_workspace(nbytes, dev)
+    o = torch.empty_like(q)
+    _native.check(_native.lib.lara_gqa_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), lens.data_ptr(),
+                                               o.data_ptr(), B, n, Hq, Hkv, D, Lmax, int(causal),
+                                               1.0 / math.sqrt(D), ws.data_ptr(), ws.numel(),
+                                               torch.cuda.current_stream().cuda_stream), "prefill")
+    torch.cuda.synchronize()
+    assert ops.workspace_status(ws) == 0
+    return o
+
+
+CASES = [
+    # (B, Hq, Hkv, D, cached, n, causal)
+    (2, 32, 8, 128, [300, 250], 40, True),
+    (1, 32, 8, 128, [0], 200, True),        # pure self-attention prefill, 2 query tiles
+    (2, 16, 2, 128, [130, 5], 129, False),  # non-causal, G=8, query tile of 1 row
+    (1, 8, 8, 128, [1000], 257, True),      # MHA, 3 query tiles
+    (2, 64, 8, 128, [513, 1024], 130, True),
+    (1, 8, 2, 64, [77], 33, True),          # head_dim 64: streaming kernel only
+]
+
+
+@pytest.mark.parametrize("path", ["tc", "stream"])
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "B{}_Hq{}_Hkv{}_D{}_c{}_n{}_{}".format(
+    c[0], c[1], c[2], c[3], max(c[4]), c[5], "causal" if c[6] else "full"))
+def test_prefill_parity(monkeypatch, path, case):
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    B, Hq, Hkv, D, cached, n, causal = case
+    if path == "tc" and D != 128:
+        pytest.skip("tensor-core kernel is for head_dim 128")
+    monkeypatch.setenv("LARA_ATTN_PATH", path)
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(B * 1000 + n)
+    Lmax = max(cached) + n + 7
+    q = (torch.randn((B, n, Hq, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, Lmax, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, Lmax, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    o = words_of(_prefill(dev, q, k, v, cached, causal))
+    qw, kw, vw = words_of(q), words_of(k), words_of(v)
+    for b in range(B):
+        c = cached[b]
+        # the new tokens' K/V sit at positions c .. c+n-1 of the cache
+        gold = oracle.prefill_attention(qw[b:b + 1].transpose(0, 2, 1, 3), kw[b:b + 1], vw[b:b + 1],
+                                        np.array([c + n]), c, causal=causal)[0]
+        g64 = oracle.prefill_attention(qw[b:b + 1].transpose(0, 2, 1, 3), kw[b:b + 1], vw[b:b + 1],
+                                       np.array([c + n]), c, causal=causal, dtype=np.float64)[0]
+        assert_bf16_parity(o[b].transpose(1, 0, 2), gold, g64, what=f"{path} b={b}")
+
+
+def test_dense_tc_matches_stream(monkeypatch):
+    """The reference transaction (Lq = Lkv = 512, bases 31/7) on both kernels."""
+    import make_golden as mg
+    from lara_b200 import ops
+
+    dev = torch.device("cuda:0")
+    q, k, v = mg.board_inputs(77, 512, oracle.fp32_to_bf16_u16)
+    t = lambda a: torch.from_numpy(a.astype(np.int16)).to(dev)  # noqa: E731
+    outs = {}
+    for path in ("tc", "stream"):
+        monkeypatch.setenv("LARA_ATTN_PATH", path)
+        outs[path] = words_of(ops.attention_dense(t(q), t(k), t(v), causal=True, q_pos_base=31, kv_pos_base=7))
+    gold = oracle.cpu_attention_numpy(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
+    for path, o in outs.items():
+        assert_bf16_parity(o, gold, what=f"dense {path}")
+
+
+@pytest.mark.slow
+def test_config5_full_size_sampled(monkeypatch):
+    """Config 5 (B=4, 2048 new over 8192 cached, causal) on the tensor-core path;
+    oracle on query rows 0-15 and 2032-2047 of every sequence."""
+    from lara_b200.workloads import PREFILL, make_prefill_inputs
+
+    monkeypatch.setenv("LARA_ATTN_PATH", "tc")
+    dev = torch.device("cuda:0")
+    cfg = PREFILL
+    q, k, v, kn, vn, lens = make_prefill_inputs(cfg, dev)
+    C, n = cfg.cached, cfg.new
+    k[:, :, C:C + n] = kn
+    v[:, :, C:C + n] = vn
+    o = words_of(_prefill(dev, q, k, v, [C] * cfg.batch, True))
+    qw = words_of(q)
+    for b in range(cfg.batch):
+        kw, vw = words_of(k[b:b + 1]), words_of(v[b:b + 1])
+        for i0 in (0, n - 16):
+            qs = qw[b:b + 1, i0:i0 + 16].transpose(0, 2, 1, 3)
+            gold = oracle.prefill_attention(qs, kw, vw, np.array([C + n]), C + i0, causal=True)[0]
+            assert_bf16_parity(o[b, i0:i0 + 16].transpose(1, 0, 2), gold, what=f"cfg5 b={b} rows {i0}+16")
