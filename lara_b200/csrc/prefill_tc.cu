@@ -14,12 +14,14 @@
 //                                           the softmax of S_j)
 //                        O  += P_j . V_j   (A = P_j read from TMEM, B = V_j MN-major)
 //                      and tcgen05.commit to mbarriers.
-//   warps 0-3        : one thread per query row (TMEM lane): load S_j, scale,
+//   warps 0-7        : two threads per query row (TMEM lane), one per half of
+//                      the 128 columns: load S_j, scale,
 //                      causal/length mask, online softmax in log2 domain (fp32
-//                      running max and sum), P_j -> bf16 (round to nearest
+//                      running max and sum; the pair exchanges row maxima
+//                      through shared memory), P_j -> bf16 (round to nearest
 //                      even) written back into the S buffer for the P.V MMA,
-//                      rescale of the O accumulator in TMEM when the row max
-//                      moved, and the epilogue O / l -> bf16 stores.
+//                      rescale of the O accumulator in TMEM when the
+//                      reference max moved, and the epilogue O / l -> bf16.
 //
 // KV tiles beyond the last key visible to any row of the tile are never
 // loaded (the causal tile skip of hw/rtl/core/attn_core.sv:138-153); the
@@ -46,7 +48,13 @@ constexpr int kHead = 128;         // head_dim
 constexpr int kHalfBytes = 128 * 128;  // one [128 rows x 64 bf16] swizzled half tile
 constexpr int kTileBytes = 2 * kHalfBytes;  // [128 x 128] bf16 as two halves
 constexpr int kStages = 2;
-constexpr int kThreads = 192;      // warps 0-3 softmax, 4 MMA, 5 TMA
+constexpr int kSoftmaxWarps = 8;   // two per TMEM lane quarter: each owns 64 of a row's 128 columns
+constexpr int kMmaWarp = kSoftmaxWarps;
+constexpr int kTmaWarp = kSoftmaxWarps + 1;
+constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
+// The reference max used for exponentiation only moves when a row's max grows
+// by more than this (log2 units), so O is rarely rescaled; p stays <= 2^8.
+constexpr float kRescaleThreshold = 8.0f;
 constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
 
 // shared memory map (offsets from a 1024-aligned base)
@@ -54,7 +62,8 @@ constexpr int kQOff = 0;
 constexpr int kKOff = kQOff + kTileBytes;                 // K stages
 constexpr int kVOff = kKOff + kStages * kTileBytes;       // V stages
 constexpr int kBarOff = kVOff + kStages * kTileBytes;
-constexpr int kSmemUsed = kBarOff + 256;
+constexpr int kRedOff = kBarOff + 256;                    // row-max / row-sum exchange [2][2][128] floats
+constexpr int kSmemUsed = kRedOff + 2 * 2 * kTileM * 4;
 constexpr int kSmemAlloc = kSmemUsed + 1024;  // + alignment slack
 
 struct Bars {
@@ -250,14 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&bars->s_full[0], 1);
     mbar_init(&bars->s_full[1], 1);
-    mbar_init(&bars->p_full, kTileM);
+    mbar_init(&bars->p_full, kSoftmaxWarps * 32);
     mbar_init(&bars->o_full, 1);
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     bars->issued = 0;
     mbar_fence_init();
   }
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&bars->tmem_base)),
                  "r"(kTmemCols)
                  : "memory");
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars->tmem_base;
   const uint32_t tm_o = tmem + 256;
 
-  if (warp == 5) {
+  if (warp == kTmaWarp) {
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
       mbar_arrive_expect_tx(&bars->q_full, kTileBytes);
@@ -289,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bars->issued = j + 1;
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       const uint32_t id_s = idesc_bf16(0);
@@ -340,11 +349,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int r = threadIdx.x;              // TMEM lane = query row within the tile
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int quarter = warp & 3;           // TMEM lane quarter
+    const int ch = warp >> 2;               // column half of S (and of O)
+    const int r = quarter * 32 + lane;      // query row within the tile
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int q_row = q0 + r;
     const long long vis_row = a.causal ? min((long long)kv_len, (long long)q_off + q_row + 1) : (long long)kv_len;
-    float m_run = -INFINITY, l_run = 0.f;
+    // every row of the tile sees keys [0, vis_min): tiles below it need no mask
+    const long long vis_min = a.causal ? min((long long)kv_len, (long long)q_off + q0 + 1) : (long long)kv_len;
+    float* red = reinterpret_cast<float*>(smem + kRedOff);  // [parity][half][row]
+    const int pair_bar = 1 + quarter;
+    float m_ref = -INFINITY, l_part = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int sb = j & 1;
@@ -355,27 +370,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float s[kTileN];
-#pragma unroll
-      for (int c = 0; c < kTileN; c += 32) tmem_ld32(tmem + lane_off + sb * 128 + c, s + c);
+      float sv[64];
+      tmem_ld32(tmem + lane_off + sb * 128 + ch * 64, sv);
+      tmem_ld32(tmem + lane_off + sb * 128 + ch * 64 + 32, sv + 32);
       tmem_wait_ld();
-      const long long vis = vis_row - (long long)j * kTileN;  // visible columns of this tile
-      float mx = -INFINITY;
+      if ((long long)(j + 1) * kTileN > vis_min) {
+        const long long vis = vis_row - (long long)j * kTileN - ch * 64;  // visible columns of this half
 #pragma unroll
-      for (int c = 0; c < kTileN; ++c) {
-        s[c] = (c < vis) ? s[c] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
+        for (int c = 0; c < 64; ++c)
+          if (c >= vis) sv[c] = -INFINITY;
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float corr = exp2f(m_run - m_use);
-      float sum = 0.f;
-      uint32_t pw[kTileN / 2];
-      uint32_t lw[kSplitP ? kTileN / 2 : 1];
+      float mx = sv[0];
 #pragma unroll
-      for (int c = 0; c < kTileN; c += 2) {
-        const float p0 = exp2f(s[c] - m_use);
-        const float p1 = exp2f(s[c + 1] - m_use);
+      for (int c = 1; c < 64; ++c) mx = fmaxf(mx, sv[c]);
+      float* rbuf = red + (j & 1) * 2 * kTileM;
+      rbuf[ch * kTileM + r] = mx;
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      mx = fmaxf(rbuf[r], rbuf[kTileM + r]);
+      const float m_tile = mx * a.scale_log2;  // scale > 0 keeps the order
+      const bool move = m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY);
+      const float m_new = move ? m_tile : m_ref;
+      const float corr = move ? exp2f(m_ref - m_new) : 1.f;
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      float sum = 0.f;
+      uint32_t pw[32];
+      uint32_t lw[kSplitP ? 32 : 1];
+#pragma unroll
+      for (int c = 0; c < 64; c += 2) {
+        const float p0 = exp2f(fmaf(sv[c], a.scale_log2, -m_use));
+        const float p1 = exp2f(fmaf(sv[c + 1], a.scale_log2, -m_use));
         sum += p0 + p1;
         const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
         pw[c / 2] = *reinterpret_cast<const uint32_t*>(&pb);
@@ -386,47 +409,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           lw[c / 2] = *reinterpret_cast<const uint32_t*>(&lb);
         }
       }
-      l_run = l_run * corr + sum;
-      // P_j (bf16 pairs along keys) into the first 64 columns of S buffer sb
-      tmem_st32(tmem + lane_off + sb * 128, pw);
-      tmem_st32(tmem + lane_off + sb * 128 + 32, pw + 32);
-      if constexpr (kSplitP) {
-        tmem_st32(tmem + lane_off + sb * 128 + 64, lw);
-        tmem_st32(tmem + lane_off + sb * 128 + 96, lw + 32);
-      }
+      l_part = l_part * corr + sum;
+      // P_j (bf16 pairs along keys): high part in columns [0,64), low part in [64,128)
+      tmem_st32(tmem + lane_off + sb * 128 + ch * 32, pw);
+      if constexpr (kSplitP) tmem_st32(tmem + lane_off + sb * 128 + 64 + ch * 32, lw);
       tmem_wait_st();
       if (j >= 1) {
-        // O holds sum_{i<j} P_i V_i at the old max once PV_{j-1} is done
+        // O holds sum_{i<j} P_i V_i at the old reference max once PV_{j-1} is done
         if (!__all_sync(0xffffffffu, wait_or_abort(&bars->o_full, (j - 1) & 1, abort))) {
           ok = false;
           break;
         }
-        tc_fence_after();
         if (__any_sync(0xffffffffu, corr != 1.f)) {
-          for (int c = 0; c < kHead; c += 32) {
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 64; c += 32) {
             float ov[32];
-            tmem_ld32(tm_o + lane_off + c, ov);
+            tmem_ld32(tm_o + lane_off + ch * 64 + c, ov);
             tmem_wait_ld();
             uint32_t ow[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) ow[i] = __float_as_uint(ov[i] * corr);
-            tmem_st32(tm_o + lane_off + c, ow);
+            tmem_st32(tm_o + lane_off + ch * 64 + c, ow);
           }
           tmem_wait_st();
         }
       }
-      m_run = m_new;
+      m_ref = m_new;
       tc_fence_before();
       mbar_arrive(&bars->p_full);
     }
-    // epilogue: O / l -> bf16
+    // epilogue: O / l -> bf16 (l = sum of the two halves' partial sums)
     if (ok && __all_sync(0xffffffffu, wait_or_abort(&bars->o_full, (ntiles - 1) & 1, abort))) {
       tc_fence_after();
-      const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
-      uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh;
-      for (int c = 0; c < kHead; c += 32) {
+      float* lbuf = red + (ntiles & 1) * 2 * kTileM;
+      lbuf[ch * kTileM + r] = l_part;
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      const float l_tot = lbuf[r] + lbuf[kTileM + r];
+      const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
+      uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh + ch * 64;
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
         float ov[32];
-        tmem_ld32(tm_o + lane_off + c, ov);
+        tmem_ld32(tm_o + lane_off + ch * 64 + c, ov);
         tmem_wait_ld();
         if (q_row < a.n_q) {
 #pragma unroll
@@ -448,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (*abort) {
     if (threadIdx.x == 0) atomicOr(a.status, kDevWaitTimeout);
     // copies issued by the TMA warp must land before the CTA retires
-    if (threadIdx.x == 5 * 32) {
+    if (threadIdx.x == kTmaWarp * 32) {
       (void)mbar_wait_bounded(&bars->q_full, 0);
       const int issued = bars->issued;
       for (int t = (issued > kStages ? issued - kStages : 0); t < issued; ++t)
@@ -456,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
