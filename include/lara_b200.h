@@ -250,7 +250,9 @@ LARA_API int lara_run_prefill_chunk(lara_ctx* ctx, const uint16_t* q, const uint
 LARA_API int lara_get_seq_lens(lara_ctx* ctx, int32_t* lens_out);
 
 /* Decode: q[B][Hq][D] -> o[B][Hq][D] over the resident cache; synchronous
- * (returns after o is written).  Replaces: run_attention's request service and
+ * (returns after o is written).  Page-locked host q / o (cudaHostAlloc,
+ * cudaHostRegister, torch pin_memory) are read and written by the kernel in
+ * place over the interconnect; pageable host memory is staged.  Replaces: run_attention's request service and
  * readback (sw/attn_driver.py:418-464) for one query token per sequence. */
 LARA_API int lara_run_query(lara_ctx* ctx, const uint16_t* q, uint16_t* o, int on_device);
 

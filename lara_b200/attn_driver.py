@@ -216,6 +216,7 @@ class AttentionAccelerator:
         self._status_word = STATUS_START_READY
         self._last_output: np.ndarray | None = None
         self._perf = LaraPerf()
+        self._max_len = 0  # longest cached sequence (profile field of run_query)
 
     # ------------------------------------------------------------------ basics
     @property
@@ -408,6 +409,7 @@ class AttentionAccelerator:
         self._require_open()
         check(lib.lara_configure_heads(self._ctx, int(batch), int(n_q_heads), int(n_kv_heads), int(head_dim),
                                        int(max_seq_len)), "configure_heads")
+        self._max_len = 0
         self.batch, self.n_q_heads, self.n_kv_heads, self.head_dim, self.max_seq_len = \
             int(batch), int(n_q_heads), int(n_kv_heads), int(head_dim), int(max_seq_len)
 
@@ -428,6 +430,7 @@ class AttentionAccelerator:
         if ln.shape != (self.batch,):
             raise ValueError(f"lens must have shape ({self.batch},)")
         check(lib.lara_kv_load(self._ctx, _ptr(kw), _ptr(vw), _ptr(ln), L, 0), "load_kv")
+        self._max_len = int(ln.max()) if ln.size else 0
 
     def append_kv(self, k_new: np.ndarray, v_new: np.ndarray) -> None:
         """Append ``k/v_new[B, Hkv, n, D]`` (or ``[B, Hkv, D]`` for one token)."""
@@ -439,6 +442,7 @@ class AttentionAccelerator:
         shape = (self.batch, self.n_kv_heads, n, self.head_dim)
         kw, vw = _words("K", k_new, shape), _words("V", v_new, shape)
         check(lib.lara_kv_append_ctx(self._ctx, _ptr(kw), _ptr(vw), n, 0), "append_kv")
+        self._max_len += n
 
     def run_query(self, q: np.ndarray, *, out: np.ndarray | None = None) -> np.ndarray:
         """Decode one query token per sequence: ``q[B, Hq, D]`` -> ``o[B, Hq, D]`` (bf16 words)."""
@@ -450,7 +454,7 @@ class AttentionAccelerator:
             out = np.empty(shape, dtype=np.uint16)
         elif out.shape != shape or out.dtype != np.uint16 or not out.flags.c_contiguous:
             raise ValueError(f"out must be a contiguous uint16 array of shape {shape}")
-        prof = self._new_profile(int(self.seq_lens.max()) if self.batch else 0, False, 0, 0)
+        prof = self._new_profile(self._max_len, False, 0, 0)
         self.last_profile = prof
         self._status_word = STATUS_BUSY
         t = time.perf_counter()
@@ -483,6 +487,7 @@ class AttentionAccelerator:
         t = time.perf_counter()
         check(lib.lara_run_prefill_chunk(self._ctx, _ptr(qw), _ptr(kw), _ptr(vw), _ptr(out), n, int(bool(causal)), 0),
               "run_prefill_chunk")
+        self._max_len += n
         prof.request_service_ms = (time.perf_counter() - t) * 1000.0
         self._last_output = out
         self._finish_profile(prof, t_start)

@@ -510,6 +510,20 @@ int ctx_ensure_ws(lara_ctx* c, size_t need) {
   return LARA_OK;
 }
 
+// Device address of page-locked host memory the GPU can address directly
+// (cudaHostAlloc / cudaHostRegister memory under unified addressing), or
+// nullptr for pageable memory.  Kernels read such inputs and write such
+// outputs over the interconnect themselves, so no staging copy is needed.
+const void* mapped_host_ptr(const void* p, size_t align) {
+  if (!aligned(p, align)) return nullptr;
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return (at.type == cudaMemoryTypeHost && at.devicePointer) ? at.devicePointer : nullptr;
+}
+
 cudaMemcpyKind in_kind(int on_device) { return on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice; }
 cudaMemcpyKind out_kind(int on_device) { return on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost; }
 
@@ -790,19 +804,26 @@ int lara_run_query(lara_ctx* c, const uint16_t* q, uint16_t* o, int on_device) {
   }
   const size_t qbytes = (size_t)c->batch * c->hq * c->d * 2;
   LARA_CUDA(cudaEventRecord(c->ev[0], c->stream));
+  // Pinned host q / o are read and written by the kernel in place; other
+  // host memory is staged through device buffers.
   const uint16_t* qd = q;
-  if (!on_device || !aligned(q, 16)) {
+  uint16_t* od = o;
+  if (!on_device) {
+    qd = static_cast<const uint16_t*>(mapped_host_ptr(q, 16));
+    od = static_cast<uint16_t*>(const_cast<void*>(mapped_host_ptr(o, 4)));
+  }
+  if (!qd || !aligned(qd, 16)) {
     LARA_CUDA(cudaMemcpyAsync(c->q_buf, q, qbytes, in_kind(on_device), c->stream));
     qd = c->q_buf;
   }
-  uint16_t* od = (on_device && aligned(o, 4)) ? o : c->o_buf;
+  if (!od || !aligned(od, 4)) od = c->o_buf;
   LARA_CUDA(cudaEventRecord(c->ev[1], c->stream));
   rc = decode_common(qd, c->k_cache, c->v_cache, c->lens_dev, od, nullptr, nullptr, c->batch, c->hq, c->hkv, c->d,
                      c->lmax, 1.0f / std::sqrt((float)c->d), c->plan_split, c->plan_chunk, c->ws, c->ws_bytes,
                      c->stream);
   if (rc) return rc;
   LARA_CUDA(cudaEventRecord(c->ev[2], c->stream));
-  if (od != o) LARA_CUDA(cudaMemcpyAsync(o, od, qbytes, out_kind(on_device), c->stream));
+  if (od == c->o_buf) LARA_CUDA(cudaMemcpyAsync(o, od, qbytes, out_kind(on_device), c->stream));
   LARA_CUDA(cudaEventRecord(c->ev[3], c->stream));
   rc = ctx_finish(c);
   if (rc) return rc;
