@@ -58,6 +58,25 @@ LARA_API int lara_abi_version(void);
 LARA_API const char* lara_last_error_string(void);
 LARA_API const char* lara_status_name(int status);
 
+/* Device facts for the deployment report.  Replaces the board readiness
+ * checks of sw/clear_pynq_cache.py:190-310 (`xbutil examine` must report a
+ * ready KV260): here the device must be visible and this library's sm_100a
+ * image must load on it (kernel_image_ok). */
+typedef struct lara_device_info {
+  char name[256];
+  char pci_bus_id[32];
+  int cc_major;
+  int cc_minor;
+  int sm_count;
+  int kernel_image_ok; /* 1 when the library's sm_100a code loads on this device */
+  int driver_version;  /* cudaDriverGetVersion, e.g. 12090 */
+  int runtime_version; /* the statically linked CUDA runtime */
+  unsigned long long total_mem_bytes;
+} lara_device_info;
+
+LARA_API int lara_device_count(int* count);
+LARA_API int lara_device_query(int device, lara_device_info* out);
+
 /* ------------------------------------------------------------------------ */
 /* Stateless kernels: caller-owned device memory (e.g. torch tensors).       */
 /* ------------------------------------------------------------------------ */

@@ -54,6 +54,12 @@ class LaraPerf(ctypes.Structure):
                 ("clock_mhz", c_double)]
 
 
+class LaraDeviceInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 256), ("pci_bus_id", ctypes.c_char * 32), ("cc_major", c_int),
+                ("cc_minor", c_int), ("sm_count", c_int), ("kernel_image_ok", c_int), ("driver_version", c_int),
+                ("runtime_version", c_int), ("total_mem_bytes", ctypes.c_ulonglong)]
+
+
 _I32P = POINTER(ctypes.c_int32)
 _U16P = POINTER(c_uint16)
 
@@ -62,6 +68,8 @@ SIGNATURES = {
     "lara_abi_version": (c_int, []),
     "lara_last_error_string": (c_char_p, []),
     "lara_status_name": (c_char_p, [c_int]),
+    "lara_device_count": (c_int, [POINTER(c_int)]),
+    "lara_device_query": (c_int, [c_int, POINTER(LaraDeviceInfo)]),
     "lara_decode_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, POINTER(c_int), POINTER(c_int)]),
     "lara_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "lara_workspace_init": (c_int, [c_void_p, c_size_t, c_void_p]),
