@@ -185,6 +185,22 @@ LARA_API int lara_attention_dense(const uint16_t* q, const uint16_t* k, const ui
                          int n_kv_heads, int head_dim, int seq_len, int q_pos_base, int kv_pos_base, int causal,
                          float scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same transaction in board arithmetic: the output words of LARA's FPGA
+ * datapath, bit for bit, for boards' expected_o comparisons
+ * (sw/board_matrix.py:118-156).  The FPGA's own fp32 adder and multiplier
+ * (hw/rtl/pkg/attn_pkg.sv:404-597), score accumulation sequential over the
+ * 128 dims, scale by fp32 0x3DB504F3, exp by a 1024-entry table with linear
+ * interpolation (hw/rtl/core/softmax_engine.sv:570-705), P truncated to bf16
+ * for P.V (hw/rtl/attn_top.sv:652-659), the O correction per 16-token block
+ * and a 256-entry reciprocal table for the normalisation
+ * (hw/rtl/mem/output_buffer.sv:199-286).  head_dim must be 128 (the scale is
+ * the RTL's constant); Hq % Hkv == 0; 0 <= pos_base, pos_base + seq_len <=
+ * 65536.  No workspace.  Stream-ordered; the first call on a device uploads
+ * the lookup tables and synchronises the stream. */
+LARA_API int lara_attention_dense_board(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
+                                        int n_q_heads, int n_kv_heads, int head_dim, int seq_len, int causal,
+                                        int q_pos_base, int kv_pos_base, void* stream);
+
 /* Decode with no allocation by the caller or the library.  Same arguments,
  * semantics and results as lara_gqa_decode, minus the workspace: the split
  * partials, arrival counters and status word live in a fixed array of
@@ -274,6 +290,16 @@ LARA_API int lara_get_seq_lens(lara_ctx* ctx, int32_t* lens_out);
  * place over the interconnect; pageable host memory is staged.  Replaces: run_attention's request service and
  * readback (sw/attn_driver.py:418-464) for one query token per sequence. */
 LARA_API int lara_run_query(lara_ctx* ctx, const uint16_t* q, uint16_t* o, int on_device);
+
+/* Arithmetic of the context's dense transactions (lara_run_attention):
+ * LARA_ARITH_IEEE (default; fp32 with a true exp, within 2 bf16 ulp of the
+ * reference's CPU golden model) or LARA_ARITH_BOARD (the FPGA's output words
+ * bit for bit, see lara_attention_dense_board; head_dim 128 only).  Decode and
+ * prefill always use IEEE arithmetic. */
+#define LARA_ARITH_IEEE 0
+#define LARA_ARITH_BOARD 1
+LARA_API int lara_set_arithmetic(lara_ctx* ctx, int mode);
+LARA_API int lara_get_arithmetic(lara_ctx* ctx);
 
 /* Dense transaction with the configure()d registers: q[Hq][L][D],
  * k/v[Hkv][L][D] -> o[Hq][L][D]; synchronous.  Replaces: run_attention

@@ -26,6 +26,9 @@ LARA_ERR_TIMEOUT = 0x21
 LARA_ERR_UNSUPPORTED = 0x22
 LARA_ERR_DEVICE = 0x23
 
+LARA_ARITH_IEEE = 0
+LARA_ARITH_BOARD = 1
+
 
 class LaraError(RuntimeError):
     """A device-side or CUDA failure reported by liblara_b200.so."""
@@ -92,6 +95,8 @@ SIGNATURES = {
     "lara_dense_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "lara_attention_dense": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                      c_int, c_int, c_float, c_void_p, c_size_t, c_void_p]),
+    "lara_attention_dense_board": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                           c_int, c_int, c_int, c_void_p]),
     "lara_create": (c_int, [c_int, POINTER(c_void_p)]),
     "lara_destroy": (c_int, [c_void_p]),
     "lara_configure_heads": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int]),
@@ -105,6 +110,8 @@ SIGNATURES = {
     "lara_read_perf": (c_int, [c_void_p, POINTER(LaraPerf)]),
     "lara_sync": (c_int, [c_void_p, c_int]),
     "lara_ctx_device": (c_int, [c_void_p]),
+    "lara_set_arithmetic": (c_int, [c_void_p, c_int]),
+    "lara_get_arithmetic": (c_int, [c_void_p]),
 }
 
 

@@ -15,6 +15,15 @@ runs hand-written sm_100a kernels.  There is no CPU fallback; constructing an
 Extensions (the north-star surface): ``configure_heads``, ``load_kv``,
 ``append_kv``, ``run_query`` (decode), ``run_prefill_chunk``, ``read_output``.
 
+Arithmetic of ``run_attention``: ``"ieee"`` (default; fp32 with a true exp,
+within 2 bf16 ulp of the reference's CPU golden model) or ``"board"`` (the
+FPGA datapath's output words bit for bit, the contract of the board case
+files' ``expected_o``).  It is chosen by the ``arithmetic`` argument, else
+the ``LARA_ARITHMETIC`` environment variable, else the ``"arithmetic"`` field
+of the deployment descriptor named by ``bitstream_path`` (written by
+``python -m lara_b200.deploy descriptors --arithmetic board``), so the
+reference harnesses select it without code changes.
+
 Timing: ``read_perf`` reports device time from CUDA events in nanoseconds,
 and ``last_profile.clock_mhz`` is 1000.0, so the harnesses' cycles/(clock*1000)
 conversion yields milliseconds (sw/board_performance.py:345-378).
@@ -35,7 +44,7 @@ from typing import Any
 
 import numpy as np
 
-from ._native import LaraPerf, check, lib
+from ._native import LARA_ARITH_BOARD, LARA_ARITH_IEEE, LaraPerf, check, lib
 
 # CSR map and status bits of the reference (sw/attn_driver.py:33-61); kept so
 # code that imports them keeps working.  The B200 status word uses the same
@@ -193,7 +202,7 @@ class AttentionAccelerator:
     """One B200 attention context (KV cache in HBM) with the reference's API."""
 
     def __init__(self, bitstream_path: str | None = None, overlay: Any | None = None, *,
-                 device: int | None = None) -> None:
+                 device: int | None = None, arithmetic: str | None = None) -> None:
         # ``bitstream_path`` identifies the deployment artefact for provenance
         # (sha256 in RunProfile), as in the reference; no file is required.
         self.bitstream_path = str(Path(bitstream_path).resolve()) if bitstream_path else None
@@ -214,6 +223,8 @@ class AttentionAccelerator:
         self.batch, self.n_q_heads, self.n_kv_heads, self.head_dim, self.max_seq_len = 1, N_Q_HEADS, N_KV_HEADS, \
             HEAD_DIM, MAX_SEQ_LEN
         self._status_word = STATUS_START_READY
+        self.arithmetic = "ieee"
+        self.set_arithmetic(arithmetic or os.environ.get("LARA_ARITHMETIC") or self._descriptor_arithmetic())
         self._last_output: np.ndarray | None = None
         self._perf = LaraPerf()
         self._max_len = 0  # longest cached sequence (profile field of run_query)
@@ -243,6 +254,24 @@ class AttentionAccelerator:
             for chunk in iter(lambda: stream.read(1024 * 1024), b""):
                 digest.update(chunk)
         return digest.hexdigest()
+
+    def _descriptor_arithmetic(self) -> str:
+        if self.bitstream_path is None:
+            return "ieee"
+        try:
+            doc = json.loads(Path(self.bitstream_path).read_text(encoding="utf-8"))
+        except (OSError, UnicodeError, ValueError):
+            return "ieee"  # not a lara_b200 descriptor: provenance only
+        return str(doc.get("arithmetic", "ieee")) if isinstance(doc, dict) else "ieee"
+
+    def set_arithmetic(self, mode: str) -> None:
+        """Select ``"ieee"`` or ``"board"`` arithmetic for ``run_attention``."""
+        self._require_open()
+        codes = {"ieee": LARA_ARITH_IEEE, "board": LARA_ARITH_BOARD}
+        if mode not in codes:
+            raise ValueError(f"arithmetic must be 'ieee' or 'board', got {mode!r}")
+        check(lib.lara_set_arithmetic(self._ctx, codes[mode]), "set_arithmetic")
+        self.arithmetic = mode
 
     def _require_open(self) -> None:
         if self._closed:

@@ -41,7 +41,8 @@ def sources() -> list[Path]:
 
 
 def headers() -> list[Path]:
-    return sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h")))
+    return sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(CSRC.glob("*.inc")) +
+                  list(INCLUDE.glob("*.h")))
 
 
 def needs_build() -> bool:

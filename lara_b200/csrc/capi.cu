@@ -456,6 +456,7 @@ struct lara_ctx {
   cudaEvent_t ev[4] = {};  // start, kernels begin, kernels end, end
   int batch = 1, hq = 32, hkv = 8, d = 128, lmax = 512;
   int seq_len = 1, q_pos_base = 0, kv_pos_base = 0, causal = 1;
+  int arithmetic = LARA_ARITH_IEEE;  // dense transactions: IEEE fp32 or board arithmetic
   uint16_t* k_cache = nullptr;
   uint16_t* v_cache = nullptr;
   int32_t* lens_dev = nullptr;
@@ -629,6 +630,18 @@ int lara_destroy(lara_ctx* c) {
 }
 
 int lara_ctx_device(lara_ctx* c) { return c ? c->device : -1; }
+
+int lara_set_arithmetic(lara_ctx* c, int mode) {
+  int rc = ctx_check(c);
+  if (rc) return rc;
+  if (mode != LARA_ARITH_IEEE && mode != LARA_ARITH_BOARD) return fail(LARA_ERR_BAD_CFG, "unknown arithmetic mode");
+  if (mode == LARA_ARITH_BOARD && c->d != 128)
+    return fail(LARA_ERR_UNSUPPORTED, "board arithmetic is defined for head_dim 128 only");
+  c->arithmetic = mode;
+  return LARA_OK;
+}
+
+int lara_get_arithmetic(lara_ctx* c) { return c ? c->arithmetic : -1; }
 
 int lara_configure_heads(lara_ctx* c, int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len) {
   int rc = ctx_check(c);
@@ -846,9 +859,12 @@ int lara_run_attention(lara_ctx* c, const uint16_t* q, const uint16_t* k, const 
     LARA_CUDA(cudaMalloc(&c->dv, (size_t)c->hkv * L * c->d * 2));
     c->dense_cap = L;
   }
-  int ns = 0, ch = 0;
-  rc = ctx_ensure_ws(c, dense_ws_bytes(c->hq, c->hkv, c->d, L, &ns, &ch));
-  if (rc) return rc;
+  const bool board = c->arithmetic == LARA_ARITH_BOARD;
+  if (!board) {
+    int ns = 0, ch = 0;
+    rc = ctx_ensure_ws(c, dense_ws_bytes(c->hq, c->hkv, c->d, L, &ns, &ch));
+    if (rc) return rc;
+  }
   const size_t qb = (size_t)c->hq * L * c->d * 2, kb = (size_t)c->hkv * L * c->d * 2;
   LARA_CUDA(cudaEventRecord(c->ev[0], c->stream));
   const uint16_t *qd = q, *kd = k, *vd = v;
@@ -860,8 +876,12 @@ int lara_run_attention(lara_ctx* c, const uint16_t* q, const uint16_t* k, const 
   }
   uint16_t* od = (on_device && aligned(o, 4)) ? o : c->dout;
   LARA_CUDA(cudaEventRecord(c->ev[1], c->stream));
-  rc = dense_common(qd, kd, vd, od, c->hq, c->hkv, c->d, L, c->q_pos_base, c->kv_pos_base, c->causal,
-                    1.0f / std::sqrt((float)c->d), c->ws, c->ws_bytes, c->stream);
+  if (board)
+    rc = lara_attention_dense_board(qd, kd, vd, od, c->hq, c->hkv, c->d, L, c->causal, c->q_pos_base,
+                                    c->kv_pos_base, c->stream);
+  else
+    rc = dense_common(qd, kd, vd, od, c->hq, c->hkv, c->d, L, c->q_pos_base, c->kv_pos_base, c->causal,
+                      1.0f / std::sqrt((float)c->d), c->ws, c->ws_bytes, c->stream);
   if (rc) return rc;
   LARA_CUDA(cudaEventRecord(c->ev[2], c->stream));
   if (od != o) LARA_CUDA(cudaMemcpyAsync(o, od, qb, out_kind(on_device), c->stream));

@@ -26,6 +26,7 @@ On B200 the deployed artefact is ``liblara_b200.so``:
 Command line::
 
     python -m lara_b200.deploy descriptors --out DIR [--name lara_attention]
+        [--arithmetic ieee|board]
     python -m lara_b200.deploy environment [--bitstream DIR/lara_attention.bit]
         [--environment-output board_environment.txt]
         [--environment-json board_environment.json]
@@ -79,8 +80,15 @@ def descriptor_paths(bitstream: Path) -> tuple[Path, Path, Path]:
     return bitstream, bitstream.with_suffix(".hwh"), bitstream.with_suffix(".xsa")
 
 
-def write_descriptors(out_dir: str | Path, name: str = DEFAULT_NAME) -> tuple[Path, Path, Path]:
-    """Write ``<name>.bit/.hwh/.xsa`` describing the built library; returns their paths."""
+def write_descriptors(out_dir: str | Path, name: str = DEFAULT_NAME, arithmetic: str = "ieee") -> tuple[Path, Path, Path]:
+    """Write ``<name>.bit/.hwh/.xsa`` describing the built library; returns their paths.
+
+    ``arithmetic`` ("ieee" or "board") is recorded in the ``.bit`` descriptor;
+    an ``AttentionAccelerator`` opened with that descriptor as its
+    ``bitstream_path`` computes ``run_attention`` in that arithmetic.
+    """
+    if arithmetic not in ("ieee", "board"):
+        raise ValueError("arithmetic must be 'ieee' or 'board'")
     from . import attn_driver as drv
     from . import build as bld
 
@@ -93,7 +101,7 @@ def write_descriptors(out_dir: str | Path, name: str = DEFAULT_NAME) -> tuple[Pa
     docs = {
         bit: {**common, "kind": "bitstream", "library": lib_path.name, "library_path": str(lib_path),
               "library_sha256": _sha256(lib_path), "library_size_bytes": lib_path.stat().st_size,
-              "abi_version": int(nat.lib.lara_abi_version())},
+              "abi_version": int(nat.lib.lara_abi_version()), "arithmetic": arithmetic},
         hwh: {**common, "kind": "hardware_handoff",
               "decode_kernel": {"head_dims": list(DECODE_HEAD_DIMS), "group_sizes": list(DECODE_GROUP_SIZES)},
               "tensor_core_kernel": {"head_dims": list(TENSOR_CORE_HEAD_DIMS)},
@@ -262,6 +270,8 @@ def main(argv: list[str] | None = None) -> int:
     d = sub.add_parser("descriptors", help="write the .bit/.hwh/.xsa descriptor trio")
     d.add_argument("--out", type=Path, default=Path("."))
     d.add_argument("--name", default=DEFAULT_NAME)
+    d.add_argument("--arithmetic", choices=("ieee", "board"), default="ieee",
+                   help="run_attention arithmetic: IEEE fp32 (default) or the FPGA's output words bit for bit")
     e = sub.add_parser("environment", help="check the device and write board_environment.{txt,json}")
     e.add_argument("--bitstream", type=Path)
     e.add_argument("--device", type=int)
@@ -270,7 +280,7 @@ def main(argv: list[str] | None = None) -> int:
     e.add_argument("--hardware-sha256-output", type=Path, default=Path("deployed_hardware_sha256.txt"))
     args = ap.parse_args(argv)
     if args.cmd == "descriptors":
-        for p in write_descriptors(args.out, args.name):
+        for p in write_descriptors(args.out, args.name, args.arithmetic):
             print(p)
         return 0
     report = environment_report(args.bitstream, args.device)

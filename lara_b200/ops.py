@@ -196,3 +196,18 @@ def attention_dense(q, k, v, *, causal=True, q_pos_base=0, kv_pos_base=0, scale=
                                    q_pos_base, kv_pos_base, int(bool(causal)), sc, ws.data_ptr(), ws.numel(),
                                    _stream(q.device)), "lara_attention_dense")
     return o
+
+
+def attention_dense_board(q, k, v, *, causal=True, q_pos_base=0, kv_pos_base=0):
+    """``attention_dense`` in board arithmetic: the FPGA datapath's output words bit for bit
+    (head_dim 128; see ``lara_attention_dense_board`` in include/lara_b200.h)."""
+    Hq, L, D = q.shape
+    Hkv = k.shape[0]
+    _check_words("q", q)
+    _check_words("k", k, (Hkv, L, D))
+    _check_words("v", v, (Hkv, L, D))
+    o = torch.empty_like(q)
+    check(lib.lara_attention_dense_board(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), Hq, Hkv, D, L,
+                                         int(bool(causal)), q_pos_base, kv_pos_base, _stream(q.device)),
+          "lara_attention_dense_board")
+    return o
