@@ -61,8 +61,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2,
-                    help="BASELINE config (2 = the headline Llama-3-8B decode; 5 = chunked prefill)")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6], default=2,
+                    help="BASELINE config (2 = the headline Llama-3-8B decode; 5 = chunked prefill); "
+                         "6 = the layer prologue (RMSNorm + QKV projection + RoPE) of config 5's new tokens")
     ap.add_argument("--batch", type=int, default=None, help="sequences per rank (default: config 2's 64)")
     ap.add_argument("--seq-len", type=int, default=None)
     ap.add_argument("--splits", type=int, default=0, help="force the split count (0 = planner)")
@@ -603,6 +604,103 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+def run_prologue(args, rank: int, world: int, local_rank: int) -> int:
+    """Config 6: the run_layer prologue of config 5's chunk on the tensor cores.
+
+    One step = RMSNorm + fused QKV projection / RoPE / head scatter for the
+    2048 new tokens of each of config 5's 4 sequences (Llama-3-8B: hidden
+    4096 -> 32 q + 8 k + 8 v heads of 128; positions 8192 + t), one launch
+    sequence per sequence.  Weights bf16 [4096][6144], N(0,1)/64."""
+    import torch
+    import torch.distributed as dist
+
+    from lara_b200 import _native, ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    B, L, hidden, hq, hkv, D, base_pos = 4, 2048, 4096, 32, 8, 128, 8192
+    n_total = (hq + 2 * hkv) * D
+    g = torch.Generator(device=dev)
+    g.manual_seed(6)
+    x = torch.randn((B, L, hidden), generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn((hidden, n_total), generator=g, device=dev) / 64.0).to(torch.bfloat16)
+    rms = (1.0 + 0.1 * torch.randn((hidden,), generator=g, device=dev)).to(torch.bfloat16)
+    q = torch.empty((B, hq, L, D), dtype=torch.bfloat16, device=dev)
+    k = torch.empty((B, hkv, L, D), dtype=torch.bfloat16, device=dev)
+    v = torch.empty_like(k)
+    nb = int(_native.lib.lara_layer_prologue_workspace_bytes(L, hidden))
+    wss = [ops.new_workspace(nb, dev) for _ in range(B)]
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for b in range(B):
+            _native.check(_native.lib.lara_layer_prologue(
+                x[b].data_ptr(), rms.data_ptr(), w.data_ptr(), q[b].data_ptr(), k[b].data_ptr(), v[b].data_ptr(),
+                L, hidden, hq, hkv, D, base_pos, base_pos, 1e-5, 10000.0, wss[b].data_ptr(), wss[b].numel(),
+                stream.cuda_stream), "layer_prologue")
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if any(ops.workspace_status(ws) != 0 for ws in wss):
+        raise RuntimeError("prologue reported a device error status")
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.start()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    sampler.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    clocks = sampler.summary()
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    if rank != 0:
+        return 0
+    flops = 2.0 * B * L * hidden * n_total
+    peak, peak_src = 1415.2, "fallback 1400 TFLOP/s sustained"
+    pp = ROOT / "MEASURED_PEAKS.json"
+    if pp.exists():
+        try:
+            peak = float(json.loads(pp.read_text())["bf16_tflops_sustained"])
+            peak_src = "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+        except (ValueError, KeyError):
+            pass
+    achieved = flops / (ms * 1e-3) / 1e12
+    line = {
+        "metric": "layer prologue TFLOP/s (RMSNorm + QKV projection + RoPE, tensor-core path)",
+        "value": round(achieved * world, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "llama3_8b_qkv_prologue_of_cfg5_chunk", "sequences_per_gpu": B, "tokens": L,
+                   "hidden": hidden, "n_q_heads": hq, "n_kv_heads": hkv, "head_dim": D, "position_base": base_pos,
+                   "weights": "bf16 [4096][6144] (50 MB, read once per launch from L2/HBM)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                     "algorithmic_flop_per_step": flops,
+                     "note": "step time includes the RMSNorm and RoPE-table kernels (3 launches per sequence)"},
+        "gpu_launches": args.steps * 3 * B, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main() -> int:
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -624,6 +722,8 @@ def main() -> int:
     try:
         if args.config == 5:
             return run_prefill(args, rank, world, local_rank)
+        if args.config == 6:
+            return run_prologue(args, rank, world, local_rank)
         return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1 and dist.is_initialized():

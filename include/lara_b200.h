@@ -201,6 +201,29 @@ LARA_API int lara_attention_dense_board(const uint16_t* q, const uint16_t* k, co
                                         int n_q_heads, int n_kv_heads, int head_dim, int seq_len, int causal,
                                         int q_pos_base, int kv_pos_base, void* stream);
 
+/* Layer prologue: the host half of AttentionAccelerator.run_layer
+ * (sw/attn_driver.py:552-586) on the GPU, writing the run_attention layout.
+ *   x_n = rms_weight ? bf16(fp32(fp32(x * inv) * rms_weight)) : x, with
+ *         inv = fp32(1 / sqrt(mean(x^2) + rms_eps)) from an fp64 mean
+ *         (hw/rtl/ext/rms_norm/rms_norm.sv:7)
+ *   [q | k | v] = x_n @ w_qkv with w_qkv = [Wq | Wk | Wv] stored
+ *         [hidden][(Hq + 2*Hkv) * D] (the [IN_DIM][OUT_DIM] weight stream of
+ *         hw/rtl/ext/qkv_projection/qkv_projection.sv), fp32 accumulation on
+ *         the tensor cores
+ *   RoPE on q at positions q_pos_base + t and on k at kv_pos_base + t:
+ *         dims (2i, 2i+1) rotate by pos * rope_base^(-2i/D)
+ *         (hw/rtl/core/rope_engine.sv:1-11), fp32
+ *   q[Hq][L][D], k[Hkv][L][D], v[Hkv][L][D] in bf16 (round to nearest even).
+ * x[L][hidden], rms_weight[hidden] (NULL: no normalisation) and w_qkv are
+ * bf16 device buffers; all pointers 16-byte aligned.  head_dim must be 128
+ * and hidden a multiple of 64.  Workspace: lara_layer_prologue_workspace_bytes
+ * (its first word is the status word, read by lara_workspace_status). */
+LARA_API size_t lara_layer_prologue_workspace_bytes(int seq_len, int hidden);
+LARA_API int lara_layer_prologue(const uint16_t* x, const uint16_t* rms_weight, const uint16_t* w_qkv, uint16_t* q,
+                                 uint16_t* k, uint16_t* v, int seq_len, int hidden, int n_q_heads, int n_kv_heads,
+                                 int head_dim, int q_pos_base, int kv_pos_base, float rms_eps, float rope_base,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* Decode with no allocation by the caller or the library.  Same arguments,
  * semantics and results as lara_gqa_decode, minus the workspace: the split
  * partials, arrival counters and status word live in a fixed array of

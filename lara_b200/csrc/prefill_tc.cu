@@ -37,8 +37,11 @@
 
 #include "common.cuh"
 #include "lara_internal.h"
+#include "tcgen05.cuh"
 
 namespace lara {
+
+using namespace tc;
 
 namespace {
 
@@ -94,119 +97,6 @@ struct TcArgs {
   float scale_log2;
   int* status;
 };
-
-// ---- tcgen05 / TMA primitives ----------------------------------------------
-
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_byte_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  uint64_t d = 0;
-  d |= (uint64_t)((smem_byte_addr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;  // 128-byte swizzle
-  return d;
-}
-
-// kind::f16 instruction descriptor: bf16 x bf16 -> f32, M = 128, N = 128.
-__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t b_mn_major) {
-  return (1u << 4)              // D format f32
-         | (1u << 7)            // A format bf16
-         | (1u << 10)           // B format bf16
-         | (b_mn_major << 16)   // B major (0 = K, 1 = MN)
-         | ((kTileN >> 3) << 17)
-         | ((kTileM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
-      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
-      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
-          "r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
-      "[%2];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
-      : "memory");
-}
-
-// Bounded wait that also gives up once another role has aborted.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = global_timer_ns();
-  while (true) {
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      *abort = 1;
-      return false;
-    }
-  }
-}
 
 // kSplitP: P = P_hi + P_lo (two bf16 terms, ~16 significant bits) and two
 // P.V MMA sets, so the result carries fp32-class P precision; without it P is
@@ -301,8 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
-      const uint32_t id_s = idesc_bf16(0);
-      const uint32_t id_pv = idesc_bf16(1);
+      const uint32_t id_s = idesc_bf16(kTileM, kTileN, 0);
+      const uint32_t id_pv = idesc_bf16(kTileM, kTileN, 1);
       const uint32_t q_base = smem_addr(q_smem);
       bool ok = wait_or_abort(&bars->q_full, 0, abort);
       for (int j = 0; ok && j <= ntiles; ++j) {
@@ -487,6 +377,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+}  // namespace
+
 // ---------------------------------------------------------------------------
 // host: tensor maps
 // ---------------------------------------------------------------------------
@@ -495,6 +387,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+namespace {
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
@@ -507,10 +400,10 @@ EncodeTiledFn encode_fn() {
   });
   return fn;
 }
+}  // namespace
 
-// bf16 tensor map; dims/strides innermost first; strides in bytes for dims 1..
-bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-              const cuuint32_t* box) {
+bool make_tensor_map_bf16(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+                          const cuuint64_t* strides, const cuuint32_t* box) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint32_t es[5] = {1, 1, 1, 1, 1};
@@ -519,10 +412,10 @@ bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
+bool tensor_maps_available() { return encode_fn() != nullptr; }
 
 bool prefill_tc_supported(int head_dim, int n_q_heads, int n_kv_heads) {
-  return head_dim == kHead && n_kv_heads > 0 && n_q_heads % n_kv_heads == 0 && encode_fn() != nullptr;
+  return head_dim == kHead && n_kv_heads > 0 && n_q_heads % n_kv_heads == 0 && tensor_maps_available();
 }
 
 cudaError_t prefill_tc_launch(const PrefillTcParams& p, cudaStream_t stream) {
@@ -538,8 +431,8 @@ cudaError_t prefill_tc_launch(const PrefillTcParams& p, cudaStream_t stream) {
   const cuuint64_t kd[3] = {(cuuint64_t)kHead, (cuuint64_t)p.kv_rows, (cuuint64_t)p.batch * p.n_kv_heads};
   const cuuint64_t ks[2] = {(cuuint64_t)kHead * 2, (cuuint64_t)p.kv_rows * kHead * 2};
   const cuuint32_t kbox[3] = {64, (cuuint32_t)kTileN, 1};
-  if (!make_map(&mq, p.q, 4, qd, qs, qbox) || !make_map(&mk, p.k, 3, kd, ks, kbox) ||
-      !make_map(&mv, p.v, 3, kd, ks, kbox))
+  if (!make_tensor_map_bf16(&mq, p.q, 4, qd, qs, qbox) || !make_tensor_map_bf16(&mk, p.k, 3, kd, ks, kbox) ||
+      !make_tensor_map_bf16(&mv, p.v, 3, kd, ks, kbox))
     return cudaErrorInvalidValue;
   TcArgs a{};
   a.n_q = p.n_q;
