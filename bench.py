@@ -609,8 +609,9 @@ def run_prologue(args, rank: int, world: int, local_rank: int) -> int:
 
     One step = RMSNorm + fused QKV projection / RoPE / head scatter for the
     2048 new tokens of each of config 5's 4 sequences (Llama-3-8B: hidden
-    4096 -> 32 q + 8 k + 8 v heads of 128; positions 8192 + t), one launch
-    sequence per sequence.  Weights bf16 [4096][6144], N(0,1)/64."""
+    4096 -> 32 q + 8 k + 8 v heads of 128; positions 8192 + t) in one batched
+    call (3 launches: RoPE table, RMSNorm, persistent projection).  Weights
+    bf16 [4096][6144], N(0,1)/64."""
     import torch
     import torch.distributed as dist
 
@@ -628,16 +629,15 @@ def run_prologue(args, rank: int, world: int, local_rank: int) -> int:
     q = torch.empty((B, hq, L, D), dtype=torch.bfloat16, device=dev)
     k = torch.empty((B, hkv, L, D), dtype=torch.bfloat16, device=dev)
     v = torch.empty_like(k)
-    nb = int(_native.lib.lara_layer_prologue_workspace_bytes(L, hidden))
-    wss = [ops.new_workspace(nb, dev) for _ in range(B)]
+    nb = int(_native.lib.lara_layer_prologue_workspace_bytes(B, L, hidden))
+    wss = [ops.new_workspace(nb, dev)]
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        for b in range(B):
-            _native.check(_native.lib.lara_layer_prologue(
-                x[b].data_ptr(), rms.data_ptr(), w.data_ptr(), q[b].data_ptr(), k[b].data_ptr(), v[b].data_ptr(),
-                L, hidden, hq, hkv, D, base_pos, base_pos, 1e-5, 10000.0, wss[b].data_ptr(), wss[b].numel(),
-                stream.cuda_stream), "layer_prologue")
+        _native.check(_native.lib.lara_layer_prologue(
+            x.data_ptr(), rms.data_ptr(), w.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            B, L, hidden, hq, hkv, D, base_pos, base_pos, 1e-5, 10000.0, wss[0].data_ptr(), wss[0].numel(),
+            stream.cuda_stream), "layer_prologue")
 
     def barrier():
         if world > 1:
@@ -694,8 +694,8 @@ def run_prologue(args, rank: int, world: int, local_rank: int) -> int:
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_flop_per_step": flops,
-                     "note": "step time includes the RMSNorm and RoPE-table kernels (3 launches per sequence)"},
-        "gpu_launches": args.steps * 3 * B, "clocks": clocks,
+                     "note": "step time includes the RMSNorm and RoPE-table kernels (3 launches per step)"},
+        "gpu_launches": args.steps * 3, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
     return 0

@@ -213,16 +213,19 @@ LARA_API int lara_attention_dense_board(const uint16_t* q, const uint16_t* k, co
  *   RoPE on q at positions q_pos_base + t and on k at kv_pos_base + t:
  *         dims (2i, 2i+1) rotate by pos * rope_base^(-2i/D)
  *         (hw/rtl/core/rope_engine.sv:1-11), fp32
- *   q[Hq][L][D], k[Hkv][L][D], v[Hkv][L][D] in bf16 (round to nearest even).
- * x[L][hidden], rms_weight[hidden] (NULL: no normalisation) and w_qkv are
- * bf16 device buffers; all pointers 16-byte aligned.  head_dim must be 128
- * and hidden a multiple of 64.  Workspace: lara_layer_prologue_workspace_bytes
- * (its first word is the status word, read by lara_workspace_status). */
-LARA_API size_t lara_layer_prologue_workspace_bytes(int seq_len, int hidden);
+ *   q[B][Hq][L][D], k[B][Hkv][L][D], v[B][Hkv][L][D] in bf16 (round to
+ *         nearest even); B = batch sequences of seq_len tokens each, every
+ *         sequence at the same position bases (B = 1 is run_layer's case).
+ * x[B][L][hidden], rms_weight[hidden] (NULL: no normalisation) and w_qkv are
+ * bf16 device buffers; all pointers 16-byte aligned.  head_dim must be 128,
+ * hidden a multiple of 64, positions below 2^24.  Workspace:
+ * lara_layer_prologue_workspace_bytes (its first word is the status word,
+ * read by lara_workspace_status). */
+LARA_API size_t lara_layer_prologue_workspace_bytes(int batch, int seq_len, int hidden);
 LARA_API int lara_layer_prologue(const uint16_t* x, const uint16_t* rms_weight, const uint16_t* w_qkv, uint16_t* q,
-                                 uint16_t* k, uint16_t* v, int seq_len, int hidden, int n_q_heads, int n_kv_heads,
-                                 int head_dim, int q_pos_base, int kv_pos_base, float rms_eps, float rope_base,
-                                 void* workspace, size_t workspace_bytes, void* stream);
+                                 uint16_t* k, uint16_t* v, int batch, int seq_len, int hidden, int n_q_heads,
+                                 int n_kv_heads, int head_dim, int q_pos_base, int kv_pos_base, float rms_eps,
+                                 float rope_base, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Decode with no allocation by the caller or the library.  Same arguments,
  * semantics and results as lara_gqa_decode, minus the workspace: the split

@@ -97,9 +97,10 @@ SIGNATURES = {
                                      c_int, c_int, c_float, c_void_p, c_size_t, c_void_p]),
     "lara_attention_dense_board": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                            c_int, c_int, c_int, c_void_p]),
-    "lara_layer_prologue_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "lara_layer_prologue_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "lara_layer_prologue": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
-                                    c_int, c_int, c_int, c_int, c_float, c_float, c_void_p, c_size_t, c_void_p]),
+                                    c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p, c_size_t,
+                                    c_void_p]),
     "lara_create": (c_int, [c_int, POINTER(c_void_p)]),
     "lara_destroy": (c_int, [c_void_p]),
     "lara_configure_heads": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int]),

@@ -28,6 +28,7 @@
 // and tensor-core work, frees TMEM and returns.
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "../../include/lara_b200.h"
@@ -41,35 +42,38 @@ using namespace tc;
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr int kBM = 128, kBN = 256, kBK = 64;
 constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;       // 16 KB: [128 tokens][64] bf16, swizzled rows of 128 B
 constexpr int kBChunk = kBK * 64 * 2;        // 8 KB: [64 k][64 n] bf16
-constexpr int kBBytes = 2 * kBChunk;         // [64 k][128 n] as two 64-column chunks
+constexpr int kBBytes = (kBN / 64) * kBChunk;  // [64 k][256 n] as four 64-column chunks
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kBarOff = kStages * kStageBytes;
 constexpr int kSmemAlloc = kBarOff + 256 + 1024;
-constexpr int kThreads = 192;                // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr uint32_t kTmemCols = 128;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = (2 + kEpiWarps) * 32;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr uint32_t kTmemCols = 2 * kBN;         // two accumulators: tile i uses columns (i & 1) * 256
 constexpr int kHead = 128;
 
 struct PBars {
   uint64_t full[kStages];
   uint64_t empty[kStages];
-  uint64_t acc_full;
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  int issued;
+  int issued;  // K slices whose copies were issued
 };
 static_assert(sizeof(PBars) <= 256, "barrier block");
 
 struct ProArgs {
-  uint16_t* q;
-  uint16_t* k;
+  uint16_t* q;             // [batch][Hq][L][D]
+  uint16_t* k;             // [batch][Hkv][L][D]
   uint16_t* v;
-  int L, nk;               // tokens, K slices of 64
-  int n_q_cols, n_kv_cols;  // Hq*D, Hkv*D
+  int L, rows, nk;          // tokens per sequence, batch * L, K slices of 64
+  int n_q_heads, n_kv_heads, n_cols;
+  int m_tiles, n_tiles;
   const float2* rope_q;     // [D/2][L] (cos, sin) at position q_pos_base + t
   const float2* rope_k;     // [D/2][L] at kv_pos_base + t
   int* status;
@@ -82,6 +86,9 @@ struct RopeArgs {
   float theta[kHead / 2];
 };
 
+// Persistent: CTA c handles tiles c, c + grid, ...; tile t covers rows
+// (t / n_tiles) * 128 and columns (t % n_tiles) * 256, so the CTAs resident at
+// one time share a few A row tiles while W stays in L2.
 __global__ void __launch_bounds__(kThreads, 1)
     qkv_rope_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     const __grid_constant__ ProArgs a) {
@@ -90,14 +97,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   PBars* bars = reinterpret_cast<PBars*>(smem + kBarOff);
   volatile int* abort = &bars->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
+  const int n_tiles_total = a.m_tiles * a.n_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
-    mbar_init(&bars->acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], kEpiWarps * 32);
+    }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     bars->issued = 0;
@@ -115,39 +125,56 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
     if (lane == 0) {
-      for (int kb = 0; kb < a.nk; ++kb) {
-        const int st = kb % kStages;
-        if (kb >= kStages && !wait_or_abort(&bars->empty[st], ((kb / kStages) - 1) & 1, abort)) break;
-        uint8_t* as = smem + st * kStageBytes;
-        uint8_t* bs = as + kABytes;
-        mbar_arrive_expect_tx(&bars->full[st], kStageBytes);
-        tma_load_2d(as, &tm_a, kb * kBK, m0, &bars->full[st]);
-        tma_load_2d(bs, &tm_b, n0, kb * kBK, &bars->full[st]);
-        tma_load_2d(bs + kBChunk, &tm_b, n0 + 64, kb * kBK, &bars->full[st]);
-        bars->issued = kb + 1;
+      int g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_tiles_total; t += gridDim.x) {
+        const int m0 = (t / a.n_tiles) * kBM, n0 = (t % a.n_tiles) * kBN;
+        for (int kb = 0; kb < a.nk; ++kb, ++g) {
+          const int st = g % kStages;
+          if (g >= kStages && !wait_or_abort(&bars->empty[st], ((g / kStages) - 1) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* as = smem + st * kStageBytes;
+          uint8_t* bs = as + kABytes;
+          mbar_arrive_expect_tx(&bars->full[st], kStageBytes);
+          tma_load_2d(as, &tm_a, kb * kBK, m0, &bars->full[st]);
+#pragma unroll
+          for (int c = 0; c < kBN / 64; ++c) tma_load_2d(bs + c * kBChunk, &tm_b, n0 + 64 * c, kb * kBK, &bars->full[st]);
+          bars->issued = g + 1;
+        }
       }
     }
   } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16(kBM, kBN, 1);
+      int g = 0, i = 0;
       bool ok = true;
-      for (int kb = 0; kb < a.nk; ++kb) {
-        const int st = kb % kStages;
-        if (!wait_or_abort(&bars->full[st], (kb / kStages) & 1, abort)) {
-          ok = false;
-          break;
-        }
+      for (int t = blockIdx.x; ok && t < n_tiles_total; t += gridDim.x, ++i) {
+        const int ab = i & 1;
+        if (i >= 2 && !wait_or_abort(&bars->acc_empty[ab], ((i >> 1) - 1) & 1, abort)) break;
         tc_fence_after();
-        const uint32_t a_base = smem_addr(smem + st * kStageBytes);
-        const uint32_t b_base = a_base + kABytes;
+        const uint32_t acc = tmem + ab * kBN;
+        for (int kb = 0; kb < a.nk; ++kb, ++g) {
+          const int st = g % kStages;
+          if (!wait_or_abort(&bars->full[st], (g / kStages) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_addr(smem + st * kStageBytes);
+          const uint32_t b_base = a_base + kABytes;
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)
-          mma_ss(tmem, desc_sw128(a_base + kk * 32, 16, 1024), desc_sw128(b_base + kk * 16 * 128, kBChunk, 1024),
-                 idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bars->empty[st]);
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_ss(acc, desc_sw128(a_base + kk * 32, 16, 1024), desc_sw128(b_base + kk * 16 * 128, kBChunk, 1024),
+                   idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&bars->empty[st]);
+        }
+        if (ok) mma_commit(&bars->acc_full[ab]);
       }
-      if (ok) mma_commit(&bars->acc_full);
       mma_commit(&bars->drain);
       (void)mbar_wait_bounded(&bars->drain, 0);
     }
@@ -155,49 +182,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 (warps 2..5 -> quarters 2,3,0,1)
     const int row = quarter * 32 + lane;
-    const int t = m0 + row;        // token
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    if (__all_sync(0xffffffffu, wait_or_abort(&bars->acc_full, 0, abort))) {
+    const int n_q_cols = a.n_q_heads * kHead, n_kv_cols = a.n_kv_heads * kHead;
+    int i = 0;
+    for (int t = blockIdx.x; t < n_tiles_total; t += gridDim.x, ++i) {
+      const int ab = i & 1;
+      if (!__all_sync(0xffffffffu, wait_or_abort(&bars->acc_full[ab], (i >> 1) & 1, abort))) break;
       tc_fence_after();
-      // which tensor / head this column tile belongs to (tiles are head-aligned: D == kBN)
-      uint16_t* dst;
-      const float2* rope = nullptr;
-      if (n0 < a.n_q_cols) {
-        dst = a.q + ((long long)(n0 / kHead) * a.L + t) * kHead;
-        rope = a.rope_q;
-      } else if (n0 < a.n_q_cols + a.n_kv_cols) {
-        dst = a.k + ((long long)((n0 - a.n_q_cols) / kHead) * a.L + t) * kHead;
-        rope = a.rope_k;
-      } else {
-        dst = a.v + ((long long)((n0 - a.n_q_cols - a.n_kv_cols) / kHead) * a.L + t) * kHead;
-      }
-      const int tr = t < a.L ? t : a.L - 1;  // rows past L are computed, not stored
-#pragma unroll
+      const int r = (t / a.n_tiles) * kBM + row;  // row of the [batch * L] token matrix
+      const int n0 = (t % a.n_tiles) * kBN;
+      const bool live = r < a.rows;
+      const int rr = live ? r : a.rows - 1;
+      const int b = rr / a.L, tok = rr % a.L;
+#pragma unroll 1
       for (int c = 0; c < kBN; c += 32) {
+        const int n = n0 + c;  // 32 columns inside one head (D = 128)
+        if (n >= a.n_cols) break;  // ragged last column tile (TMA filled it with zeros)
+        uint16_t* dst;
+        const float2* rope = nullptr;
+        if (n < n_q_cols) {
+          dst = a.q + (((long long)b * a.n_q_heads + n / kHead) * a.L + tok) * kHead + (n % kHead);
+          rope = a.rope_q;
+        } else if (n < n_q_cols + n_kv_cols) {
+          dst = a.k + (((long long)b * a.n_kv_heads + (n - n_q_cols) / kHead) * a.L + tok) * kHead + (n % kHead);
+          rope = a.rope_k;
+        } else {
+          const int nv = n - n_q_cols - n_kv_cols;
+          dst = a.v + (((long long)b * a.n_kv_heads + nv / kHead) * a.L + tok) * kHead + (nv % kHead);
+        }
         float x[32];
-        tmem_ld32(tmem + lane_off + c, x);
+        tmem_ld32(tmem + lane_off + ab * kBN + c, x);
         tmem_wait_ld();
         if (rope) {
+          const int p0 = (n % kHead) >> 1;
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float2 cs = __ldg(rope + (long long)((c + i) >> 1) * a.L + tr);  // lanes: consecutive tokens
-            const float x0 = x[i], x1 = x[i + 1];
-            x[i] = x0 * cs.x - x1 * cs.y;
-            x[i + 1] = x0 * cs.y + x1 * cs.x;
+          for (int j = 0; j < 32; j += 2) {
+            const float2 cs = __ldg(rope + (long long)(p0 + (j >> 1)) * a.L + tok);  // lanes: consecutive tokens
+            const float x0 = x[j], x1 = x[j + 1];
+            x[j] = x0 * cs.x - x1 * cs.y;
+            x[j + 1] = x0 * cs.y + x1 * cs.x;
           }
         }
-        if (t < a.L) {
+        if (live) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
+          for (int j = 0; j < 32; j += 8) {
             uint4 w;
-            w.x = pack2_bf16(x[i], x[i + 1]);
-            w.y = pack2_bf16(x[i + 2], x[i + 3]);
-            w.z = pack2_bf16(x[i + 4], x[i + 5]);
-            w.w = pack2_bf16(x[i + 6], x[i + 7]);
-            *reinterpret_cast<uint4*>(dst + c + i) = w;
+            w.x = pack2_bf16(x[j], x[j + 1]);
+            w.y = pack2_bf16(x[j + 2], x[j + 3]);
+            w.z = pack2_bf16(x[j + 4], x[j + 5]);
+            w.w = pack2_bf16(x[j + 6], x[j + 7]);
+            *reinterpret_cast<uint4*>(dst + j) = w;
           }
         }
       }
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty[ab]);
     }
   }
 
@@ -207,8 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) atomicOr(a.status, kDevWaitTimeout);
     if (threadIdx.x == 0) {
       const int issued = bars->issued;
-      for (int kb = (issued > kStages ? issued - kStages : 0); kb < issued; ++kb)
-        (void)mbar_wait_bounded(&bars->full[kb % kStages], (kb / kStages) & 1);
+      for (int g = (issued > kStages ? issued - kStages : 0); g < issued; ++g)
+        (void)mbar_wait_bounded(&bars->full[g % kStages], (g / kStages) & 1);
     }
   }
   __syncthreads();
@@ -276,10 +315,10 @@ constexpr size_t kStatusBytes = 256;
 
 }  // namespace
 
-// workspace: status word | x_n bf16 [L][hidden] | rope tables 2 x [D/2][L] float2
-size_t prologue_workspace_bytes(int seq_len, int hidden) {
-  if (seq_len < 1 || hidden < 1) return 0;
-  const size_t xn = ((size_t)seq_len * hidden * 2 + 255) / 256 * 256;
+// workspace: status word | x_n bf16 [batch * L][hidden] | rope tables 2 x [D/2][L] float2
+size_t prologue_workspace_bytes(int batch, int seq_len, int hidden) {
+  if (batch < 1 || seq_len < 1 || hidden < 1) return 0;
+  const size_t xn = ((size_t)batch * seq_len * hidden * 2 + 255) / 256 * 256;
   return kStatusBytes + xn + 2 * (size_t)(kHead / 2) * seq_len * sizeof(float2);
 }
 
@@ -287,19 +326,22 @@ size_t prologue_workspace_bytes(int seq_len, int hidden) {
 
 using namespace lara;
 
-extern "C" size_t lara_layer_prologue_workspace_bytes(int seq_len, int hidden) {
-  return prologue_workspace_bytes(seq_len, hidden);
+extern "C" size_t lara_layer_prologue_workspace_bytes(int batch, int seq_len, int hidden) {
+  return prologue_workspace_bytes(batch, seq_len, hidden);
 }
 
 extern "C" int lara_layer_prologue(const uint16_t* x, const uint16_t* rms_weight, const uint16_t* w_qkv, uint16_t* q,
-                                   uint16_t* k, uint16_t* v, int seq_len, int hidden, int n_q_heads, int n_kv_heads,
-                                   int head_dim, int q_pos_base, int kv_pos_base, float rms_eps, float rope_base,
-                                   void* workspace, size_t workspace_bytes, void* stream) {
+                                   uint16_t* k, uint16_t* v, int batch, int seq_len, int hidden, int n_q_heads,
+                                   int n_kv_heads, int head_dim, int q_pos_base, int kv_pos_base, float rms_eps,
+                                   float rope_base, void* workspace, size_t workspace_bytes, void* stream) {
   if (head_dim != kHead)
     return set_last_error(LARA_ERR_UNSUPPORTED, "the fused projection kernel is built for head_dim 128");
-  if (seq_len < 1 || hidden < kBK || hidden % kBK || n_q_heads < 1 || n_kv_heads < 1 || n_q_heads % n_kv_heads)
+  if (batch < 1 || seq_len < 1 || hidden < kBK || hidden % kBK || n_q_heads < 1 || n_kv_heads < 1 ||
+      n_q_heads % n_kv_heads || (long long)batch * seq_len > (1ll << 30))
     return set_last_error(LARA_ERR_BAD_CFG, "bad prologue geometry (hidden must be a positive multiple of 64)");
   if (!(rms_eps >= 0.f) || !(rope_base > 1.f)) return set_last_error(LARA_ERR_BAD_CFG, "bad eps or RoPE base");
+  if (q_pos_base < 0 || kv_pos_base < 0 || q_pos_base + seq_len > (1 << 24) || kv_pos_base + seq_len > (1 << 24))
+    return set_last_error(LARA_ERR_BAD_CFG, "positions must lie in [0, 2^24) (exact in fp32)");
   if (!x || !w_qkv || !q || !k || !v || !workspace)
     return set_last_error(LARA_ERR_STREAM_DEST, "null pointer");
   const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_qkv) |
@@ -307,14 +349,15 @@ extern "C" int lara_layer_prologue(const uint16_t* x, const uint16_t* rms_weight
                        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(workspace) |
                        reinterpret_cast<uintptr_t>(rms_weight);
   if (al & 15) return set_last_error(LARA_ERR_STREAM_DEST, "buffers must be 16-byte aligned");
-  if (workspace_bytes < prologue_workspace_bytes(seq_len, hidden))
+  if (workspace_bytes < prologue_workspace_bytes(batch, seq_len, hidden))
     return set_last_error(LARA_ERR_RESULT_LEN, "prologue workspace too small");
   if (!tensor_maps_available()) return set_last_error(LARA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rows = batch * seq_len;
   int* status = static_cast<int*>(workspace);
   uint8_t* wsb = static_cast<uint8_t*>(workspace);
   uint16_t* xn = reinterpret_cast<uint16_t*>(wsb + kStatusBytes);
-  float2* rope_q = reinterpret_cast<float2*>(wsb + kStatusBytes + ((size_t)seq_len * hidden * 2 + 255) / 256 * 256);
+  float2* rope_q = reinterpret_cast<float2*>(wsb + kStatusBytes + ((size_t)rows * hidden * 2 + 255) / 256 * 256);
   float2* rope_k = q_pos_base == kv_pos_base ? rope_q : rope_q + (size_t)(kHead / 2) * seq_len;
   RopeArgs r{};
   r.rope_q = rope_q;
@@ -327,12 +370,12 @@ extern "C" int lara_layer_prologue(const uint16_t* x, const uint16_t* rms_weight
   rope_table_kernel<<<(n_rope + 255) / 256, 256, 0, st>>>(r);
   const uint16_t* a_src = x;
   if (rms_weight) {
-    rmsnorm_kernel<<<seq_len, 256, 0, st>>>(x, rms_weight, xn, hidden, rms_eps);
+    rmsnorm_kernel<<<rows, 256, 0, st>>>(x, rms_weight, xn, hidden, rms_eps);
     a_src = xn;
   }
   const int n_total = (n_q_heads + 2 * n_kv_heads) * kHead;
   CUtensorMap ma, mb;
-  const cuuint64_t ad[2] = {(cuuint64_t)hidden, (cuuint64_t)seq_len};
+  const cuuint64_t ad[2] = {(cuuint64_t)hidden, (cuuint64_t)rows};
   const cuuint64_t as[1] = {(cuuint64_t)hidden * 2};
   const cuuint32_t abox[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
   const cuuint64_t bd[2] = {(cuuint64_t)n_total, (cuuint64_t)hidden};
@@ -345,15 +388,20 @@ extern "C" int lara_layer_prologue(const uint16_t* x, const uint16_t* rms_weight
   a.k = k;
   a.v = v;
   a.L = seq_len;
+  a.rows = rows;
   a.nk = hidden / kBK;
-  a.n_q_cols = n_q_heads * kHead;
-  a.n_kv_cols = n_kv_heads * kHead;
+  a.n_q_heads = n_q_heads;
+  a.n_kv_heads = n_kv_heads;
+  a.n_cols = n_total;
+  a.m_tiles = (rows + kBM - 1) / kBM;
+  a.n_tiles = (n_total + kBN - 1) / kBN;
   a.rope_q = rope_q;
   a.rope_k = rope_k;
   a.status = status;
   cudaError_t e = cudaFuncSetAttribute(qkv_rope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
   if (e != cudaSuccess) return set_last_error(LARA_ERR_CUDA, std::string("prologue: ") + cudaGetErrorString(e));
-  dim3 grid((seq_len + kBM - 1) / kBM, n_total / kBN);
+  const long long tiles = (long long)a.m_tiles * a.n_tiles;
+  const int grid = (int)std::min<long long>(tiles, (long long)device_sm_count());
   qkv_rope_kernel<<<grid, kThreads, kSmemAlloc, st>>>(ma, mb, a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_last_error(LARA_ERR_CUDA, std::string("prologue launch: ") + cudaGetErrorString(e));

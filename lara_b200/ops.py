@@ -217,23 +217,25 @@ def layer_prologue(x, w_qkv, rms_weight=None, *, n_q_heads=32, n_kv_heads=8, hea
                    kv_pos_base=0, rms_eps=1e-5, rope_base=10000.0):
     """RMSNorm -> QKV projection -> RoPE on device tensors (``lara_layer_prologue``).
 
-    x: bf16 [L, hidden]; w_qkv: bf16 [hidden, (Hq + 2 Hkv) * D] (= [Wq | Wk | Wv]);
-    rms_weight: bf16 [hidden] or None.  Returns bf16 q [Hq, L, D], k [Hkv, L, D], v [Hkv, L, D].
+    x: bf16 [L, hidden] or [B, L, hidden]; w_qkv: bf16 [hidden, (Hq + 2 Hkv) * D] (= [Wq | Wk | Wv]);
+    rms_weight: bf16 [hidden] or None.  Returns bf16 q [(B,) Hq, L, D], k [(B,) Hkv, L, D], v likewise.
     """
-    L, hidden = x.shape
+    batched = x.dim() == 3
+    B, L, hidden = x.shape if batched else (1, *x.shape)
     n_total = (n_q_heads + 2 * n_kv_heads) * head_dim
-    _check_words("x", x, (L, hidden))
+    _check_words("x", x, tuple(x.shape))
     _check_words("w_qkv", w_qkv, (hidden, n_total))
     if rms_weight is not None:
         _check_words("rms_weight", rms_weight, (hidden,))
     dev = x.device
-    q = torch.empty((n_q_heads, L, head_dim), dtype=x.dtype, device=dev)
-    k = torch.empty((n_kv_heads, L, head_dim), dtype=x.dtype, device=dev)
+    lead = (B,) if batched else ()
+    q = torch.empty((*lead, n_q_heads, L, head_dim), dtype=x.dtype, device=dev)
+    k = torch.empty((*lead, n_kv_heads, L, head_dim), dtype=x.dtype, device=dev)
     v = torch.empty_like(k)
-    nbytes = int(lib.lara_layer_prologue_workspace_bytes(L, hidden))
+    nbytes = int(lib.lara_layer_prologue_workspace_bytes(B, L, hidden))
     ws = new_workspace(nbytes, dev)
     check(lib.lara_layer_prologue(x.data_ptr(), 0 if rms_weight is None else rms_weight.data_ptr(), w_qkv.data_ptr(),
-                                  q.data_ptr(), k.data_ptr(), v.data_ptr(), L, hidden, n_q_heads, n_kv_heads,
+                                  q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, hidden, n_q_heads, n_kv_heads,
                                   head_dim, q_pos_base, kv_pos_base, float(rms_eps), float(rope_base),
                                   ws.data_ptr(), ws.numel(), _stream(dev)), "lara_layer_prologue")
     return q, k, v

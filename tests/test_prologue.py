@@ -71,6 +71,7 @@ CASES = [
     (128, 512, 4, 4, False, 0, 0),
     (300, 4096, 32, 8, True, 3, 3),        # Llama-3-8B projection, 3 token tiles (last ragged)
     (16, 4096, 32, 8, True, 65000, 65000),  # large positions (angles up to ~6.5e4 rad)
+    (40, 128, 1, 1, True, 5, 9),            # 3 heads: a ragged 128-column last tile
 ]
 
 
@@ -115,13 +116,36 @@ def test_rmsnorm_words_bit_exact():
     q = torch.empty((4, L, 128), dtype=torch.int16, device=dev)
     k = torch.empty((2, L, 128), dtype=torch.int16, device=dev)
     v = torch.empty_like(k)
-    nb = int(_native.lib.lara_layer_prologue_workspace_bytes(L, hidden))
+    nb = int(_native.lib.lara_layer_prologue_workspace_bytes(1, L, hidden))
     ws = ops.new_workspace(nb, dev)
     _native.check(_native.lib.lara_layer_prologue(xd.data_ptr(), gd.data_ptr(), wd.data_ptr(), q.data_ptr(),
-                                                  k.data_ptr(), v.data_ptr(), L, hidden, 4, 2, 128, 0, 0, 1e-5,
+                                                  k.data_ptr(), v.data_ptr(), 1, L, hidden, 4, 2, 128, 0, 0, 1e-5,
                                                   10000.0, ws.data_ptr(), ws.numel(),
                                                   torch.cuda.current_stream().cuda_stream), "prologue")
     torch.cuda.synchronize()
     assert ops.workspace_status(ws) == 0
     xn = words_of(ws[256:256 + L * hidden * 2].view(torch.int16)).reshape(L, hidden)
     np.testing.assert_array_equal(xn, prologue.rms_norm(x, g, 1e-5))
+
+
+@pytest.mark.gpu
+def test_prologue_batched_equals_per_sequence():
+    """batch = 3 in one launch gives each sequence's single-sequence words."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    from lara_b200 import ops
+    from parity import words_of
+
+    L, hidden = 150, 256
+    rng = np.random.default_rng(8)
+    xs = _words(rng.standard_normal((3, L, hidden)))
+    _, w, g = _case(9, L, hidden, 8, 2, 1.0 / 16)
+    dev = torch.device("cuda:0")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(dev)  # noqa: E731
+    qb, kb, vb = ops.layer_prologue(t(xs), t(w), t(g), n_q_heads=8, n_kv_heads=2, q_pos_base=100, kv_pos_base=90)
+    for b in range(3):
+        q1, k1, v1 = ops.layer_prologue(t(xs[b]), t(w), t(g), n_q_heads=8, n_kv_heads=2, q_pos_base=100,
+                                        kv_pos_base=90)
+        for got, want in ((qb[b], q1), (kb[b], k1), (vb[b], v1)):
+            np.testing.assert_array_equal(words_of(got), words_of(want))
