@@ -333,6 +333,18 @@ LARA_API int lara_get_arithmetic(lara_ctx* ctx);
 LARA_API int lara_run_attention(lara_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
                        int on_device);
 
+/* One layer: lara_layer_prologue on x[L][hidden] with w_qkv / rms_weight
+ * (rms_weight may be NULL), then the dense transaction of lara_run_attention
+ * on the produced q/k/v with the configure()d registers and the context's
+ * arithmetic -> o[Hq][L][D]; synchronous.  Pointers are host memory unless
+ * on_device != 0.  Replaces: run_layer (sw/attn_driver.py:552-586), whose
+ * RMSNorm / projection / RoPE ran on the host CPU.  lara_read_perf then covers
+ * the whole call; lara_read_layer_perf splits the device time into the
+ * prologue kernels and the attention kernels. */
+LARA_API int lara_run_layer(lara_ctx* ctx, const uint16_t* x, const uint16_t* w_qkv, const uint16_t* rms_weight,
+                            int hidden, uint16_t* o, float rms_eps, float rope_base, int on_device);
+LARA_API int lara_read_layer_perf(lara_ctx* ctx, uint64_t* prologue_ns, uint64_t* attention_ns);
+
 /* Replaces: read_perf (sw/attn_driver.py:466-467, CSRs 0x100/0x108/0x10C). */
 LARA_API int lara_read_perf(lara_ctx* ctx, lara_perf* out);
 

@@ -112,6 +112,8 @@ SIGNATURES = {
     "lara_run_query": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
     "lara_run_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int]),
     "lara_read_perf": (c_int, [c_void_p, POINTER(LaraPerf)]),
+    "lara_run_layer": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_float, c_int]),
+    "lara_read_layer_perf": (c_int, [c_void_p, POINTER(c_uint64), POINTER(c_uint64)]),
     "lara_sync": (c_int, [c_void_p, c_int]),
     "lara_ctx_device": (c_int, [c_void_p]),
     "lara_set_arithmetic": (c_int, [c_void_p, c_int]),

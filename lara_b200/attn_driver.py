@@ -431,6 +431,66 @@ class AttentionAccelerator:
         self._finish_profile(prof, t_start)
         return out
 
+    def run_layer(self, hidden_states: np.ndarray, wq: np.ndarray, wk: np.ndarray, wv: np.ndarray,
+                  rms_weight: np.ndarray | None = None, *, q_pos_base: int = 0, kv_pos_base: int = 0,
+                  causal: bool = True, timeout_ms: int | None = None) -> np.ndarray:
+        """RMSNorm + QKV projection + RoPE, then attention; returns float32 ``[L, Hq * D]``.
+
+        Same call and result layout as sw/attn_driver.py:552-586, but the
+        prologue runs on the GPU (``lara_run_layer``): hidden_states
+        ``[L, hidden]``, wq ``[hidden, Hq*D]``, wk/wv ``[hidden, Hkv*D]`` (the
+        [IN][OUT] layout, Q = X @ Wq) and rms_weight ``[hidden]`` are packed to
+        bf16; RMSNorm (eps 1e-5), the projection (fp32 accumulation) and RoPE
+        (base 10000, dim pairs (2i, 2i+1), positions q/kv_pos_base + t) run in
+        one fused launch sequence, and the attention uses this context's
+        arithmetic.  RMSNorm and RoPE are fused into the projection kernels, so
+        their device time is inside ``host_qkv_projection_ms`` and the
+        ``host_rms_norm_ms`` / ``host_rope_ms`` fields stay 0.
+        """
+        self._require_open()
+        t_start = time.perf_counter()
+        x = np.asarray(hidden_states)
+        if x.ndim != 2:
+            raise ValueError(f"hidden_states must be [L, hidden], got {x.shape}")
+        L, hidden = x.shape
+        self._validate_len(L)
+        nq, nkv = self.n_q_heads * self.head_dim, self.n_kv_heads * self.head_dim
+        for name, w, cols in (("wq", wq, nq), ("wk", wk, nkv), ("wv", wv, nkv)):
+            if tuple(np.shape(w)) != (hidden, cols):
+                raise ValueError(f"expected {name}={(hidden, cols)}; got {np.shape(w)}")
+        if rms_weight is not None and tuple(np.shape(rms_weight)) != (hidden,):
+            raise ValueError(f"expected rms_weight=({hidden},); got {np.shape(rms_weight)}")
+        if hidden % 64:
+            raise ValueError("hidden size must be a multiple of 64")
+        prof = self._new_profile(L, causal, q_pos_base, kv_pos_base)
+        self.last_profile = prof
+        t = time.perf_counter()
+        xw = np.ascontiguousarray(fp32_to_bf16_u16(x))
+        w_qkv = np.ascontiguousarray(np.concatenate([fp32_to_bf16_u16(np.asarray(w)) for w in (wq, wk, wv)], axis=1))
+        gw = None if rms_weight is None else np.ascontiguousarray(fp32_to_bf16_u16(np.asarray(rms_weight)))
+        prof.input_pack_ms = (time.perf_counter() - t) * 1000.0
+        self.configure(L, q_pos_base=q_pos_base, kv_pos_base=kv_pos_base, causal=causal)
+        self.clear_status()
+        out = np.empty((self.n_q_heads, L, self.head_dim), dtype=np.uint16)
+        self._status_word = STATUS_BUSY
+        t = time.perf_counter()
+        check(lib.lara_run_layer(self._ctx, _ptr(xw), _ptr(w_qkv), None if gw is None else _ptr(gw), int(hidden),
+                                 _ptr(out), 1e-5, 10000.0, 0), "run_layer")
+        prof.request_service_ms = (time.perf_counter() - t) * 1000.0
+        self._status_word = STATUS_DONE | STATUS_START_READY
+        if timeout_ms is not None and prof.request_service_ms > timeout_ms:
+            raise TimeoutError("attention accelerator timed out while running the layer")
+        self._last_output = out
+        self._finish_profile(prof, t_start)
+        pro, att = ctypes.c_uint64(0), ctypes.c_uint64(0)
+        check(lib.lara_read_layer_perf(self._ctx, ctypes.byref(pro), ctypes.byref(att)), "read_layer_perf")
+        prof.host_rms_norm_ms = 0.0
+        prof.host_qkv_projection_ms = pro.value / 1e6
+        prof.host_rope_ms = 0.0
+        result = bf16_u16_to_fp32(out).transpose(1, 0, 2).reshape(L, nq)
+        prof.layer_total_ms = (time.perf_counter() - t_start) * 1000.0
+        return result
+
     # -------------------------------------------------------------- extensions
     def configure_heads(self, n_q_heads: int = N_Q_HEADS, n_kv_heads: int = N_KV_HEADS, head_dim: int = HEAD_DIM,
                         max_seq_len: int = MAX_SEQ_LEN, batch: int = 1) -> None:

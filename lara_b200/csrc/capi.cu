@@ -453,7 +453,7 @@ int lara_attention_dense(const uint16_t* q, const uint16_t* k, const uint16_t* v
 struct lara_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
-  cudaEvent_t ev[4] = {};  // start, kernels begin, kernels end, end
+  cudaEvent_t ev[5] = {};  // start, kernels begin, kernels end, end; [4] = prologue end (run_layer)
   int batch = 1, hq = 32, hkv = 8, d = 128, lmax = 512;
   int seq_len = 1, q_pos_base = 0, kv_pos_base = 0, causal = 1;
   int arithmetic = LARA_ARITH_IEEE;  // dense transactions: IEEE fp32 or board arithmetic
@@ -478,6 +478,13 @@ struct lara_ctx {
   void* ws = nullptr;
   size_t ws_bytes = 0;
   int* status_host = nullptr;  // pinned
+  uint16_t* lx = nullptr;      // run_layer: x [L][hidden], w_qkv [hidden][(Hq+2Hkv)D], rms weight [hidden]
+  uint16_t* lw = nullptr;
+  uint16_t* lg = nullptr;
+  size_t lx_cap = 0, lw_cap = 0, lg_cap = 0;
+  void* lws = nullptr;          // prologue workspace (status word first)
+  size_t lws_bytes = 0;
+  uint64_t layer_prologue_ns = 0, layer_attention_ns = 0;
   int plan_split = 0, plan_chunk = 0;
   bool plan_valid = false;
   lara_perf perf{};
@@ -599,7 +606,7 @@ int lara_create(int device, lara_ctx** out) {
   lara_ctx* c = new lara_ctx();
   c->device = device;
   cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-  for (int i = 0; i < 4 && e == cudaSuccess; ++i) e = cudaEventCreate(&c->ev[i]);
+  for (int i = 0; i < 5 && e == cudaSuccess; ++i) e = cudaEventCreate(&c->ev[i]);
   if (e == cudaSuccess) e = cudaMallocHost(&c->status_host, sizeof(int));
   if (e != cudaSuccess) {
     lara_destroy(c);
@@ -621,6 +628,7 @@ int lara_destroy(lara_ctx* c) {
   ctx_free_cache(c);
   ctx_free_dense(c);
   cudaFree(c->ws);
+  cudaFree(c->lx); cudaFree(c->lw); cudaFree(c->lg); cudaFree(c->lws);
   if (c->status_host) cudaFreeHost(c->status_host);
   for (auto& ev : c->ev)
     if (ev) cudaEventDestroy(ev);
@@ -889,6 +897,114 @@ int lara_run_attention(lara_ctx* c, const uint16_t* q, const uint16_t* k, const 
   rc = ctx_finish(c);
   if (rc) return rc;
   ctx_record_perf(c);
+  return LARA_OK;
+}
+
+namespace {
+// grow-only device buffer
+int ensure_buf(void** p, size_t* cap, size_t need) {
+  if (*cap >= need) return LARA_OK;
+  cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  const cudaError_t e = cudaMalloc(p, need);
+  if (e != cudaSuccess) return lara::set_last_error(LARA_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+  *cap = need;
+  return LARA_OK;
+}
+}  // namespace
+
+int lara_run_layer(lara_ctx* c, const uint16_t* x, const uint16_t* w_qkv, const uint16_t* rms_weight, int hidden,
+                   uint16_t* o, float rms_eps, float rope_base, int on_device) {
+  int rc = ctx_check(c);
+  if (rc) return rc;
+  if (!x || !w_qkv || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
+  if (hidden < 64 || hidden % 64) return fail(LARA_ERR_BAD_CFG, "hidden must be a positive multiple of 64");
+  if (c->d != 128) return fail(LARA_ERR_UNSUPPORTED, "run_layer's fused projection is built for head_dim 128");
+  DeviceGuard g(c->device);
+  const int L = c->seq_len;
+  const size_t n_total = (size_t)(c->hq + 2 * c->hkv) * c->d;
+  if (c->dense_cap < L) {
+    ctx_free_dense(c);
+    LARA_CUDA(cudaMalloc(&c->dq, (size_t)c->hq * L * c->d * 2));
+    LARA_CUDA(cudaMalloc(&c->dout, (size_t)c->hq * L * c->d * 2));
+    LARA_CUDA(cudaMalloc(&c->dk, (size_t)c->hkv * L * c->d * 2));
+    LARA_CUDA(cudaMalloc(&c->dv, (size_t)c->hkv * L * c->d * 2));
+    c->dense_cap = L;
+  }
+  const bool board = c->arithmetic == LARA_ARITH_BOARD;
+  if (!board) {
+    int ns = 0, ch = 0;
+    rc = ctx_ensure_ws(c, dense_ws_bytes(c->hq, c->hkv, c->d, L, &ns, &ch));
+    if (rc) return rc;
+  }
+  const size_t xb = (size_t)L * hidden * 2, wb = (size_t)hidden * n_total * 2, gb = (size_t)hidden * 2;
+  const size_t need_ws = lara_layer_prologue_workspace_bytes(1, L, hidden);
+  if (c->lws_bytes < need_ws) {
+    rc = ensure_buf(&c->lws, &c->lws_bytes, need_ws);
+    if (rc) return rc;
+    LARA_CUDA(cudaMemsetAsync(c->lws, 0, c->lws_bytes, c->stream));
+  }
+  const bool dev_ok = on_device && aligned(x, 16) && aligned(w_qkv, 16) && (!rms_weight || aligned(rms_weight, 16));
+  if (!dev_ok) {
+    rc = ensure_buf(reinterpret_cast<void**>(&c->lx), &c->lx_cap, xb);
+    if (!rc) rc = ensure_buf(reinterpret_cast<void**>(&c->lw), &c->lw_cap, wb);
+    if (!rc && rms_weight) rc = ensure_buf(reinterpret_cast<void**>(&c->lg), &c->lg_cap, gb);
+    if (rc) return rc;
+  }
+  LARA_CUDA(cudaEventRecord(c->ev[0], c->stream));
+  const uint16_t *xd = x, *wd = w_qkv, *gd = rms_weight;
+  if (!dev_ok) {
+    LARA_CUDA(cudaMemcpyAsync(c->lx, x, xb, in_kind(on_device), c->stream));
+    LARA_CUDA(cudaMemcpyAsync(c->lw, w_qkv, wb, in_kind(on_device), c->stream));
+    if (rms_weight) LARA_CUDA(cudaMemcpyAsync(c->lg, rms_weight, gb, in_kind(on_device), c->stream));
+    xd = c->lx;
+    wd = c->lw;
+    gd = rms_weight ? c->lg : nullptr;
+  }
+  LARA_CUDA(cudaEventRecord(c->ev[1], c->stream));
+  rc = lara_layer_prologue(xd, gd, wd, c->dq, c->dk, c->dv, 1, L, hidden, c->hq, c->hkv, c->d, c->q_pos_base,
+                           c->kv_pos_base, rms_eps, rope_base, c->lws, c->lws_bytes, c->stream);
+  if (rc) return rc;
+  LARA_CUDA(cudaEventRecord(c->ev[4], c->stream));
+  uint16_t* od = (on_device && aligned(o, 4)) ? o : c->dout;
+  if (board)
+    rc = lara_attention_dense_board(c->dq, c->dk, c->dv, od, c->hq, c->hkv, c->d, L, c->causal, c->q_pos_base,
+                                    c->kv_pos_base, c->stream);
+  else
+    rc = dense_common(c->dq, c->dk, c->dv, od, c->hq, c->hkv, c->d, L, c->q_pos_base, c->kv_pos_base, c->causal,
+                      1.0f / std::sqrt((float)c->d), c->ws, c->ws_bytes, c->stream);
+  if (rc) return rc;
+  LARA_CUDA(cudaEventRecord(c->ev[2], c->stream));
+  if (od != o) LARA_CUDA(cudaMemcpyAsync(o, od, (size_t)c->hq * L * c->d * 2, out_kind(on_device), c->stream));
+  LARA_CUDA(cudaEventRecord(c->ev[3], c->stream));
+  // prologue status word, then the attention workspace's
+  LARA_CUDA(cudaMemcpyAsync(c->status_host, c->lws, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  LARA_CUDA(cudaStreamSynchronize(c->stream));
+  if (*c->status_host) {
+    const int bits = *c->status_host;
+    LARA_CUDA(cudaMemsetAsync(c->lws, 0, sizeof(int), c->stream));
+    LARA_CUDA(cudaStreamSynchronize(c->stream));
+    return fail((bits & lara::kDevWaitTimeout) ? LARA_ERR_TIMEOUT : LARA_ERR_DEVICE, "prologue device status 0x%x",
+                bits);
+  }
+  rc = ctx_finish(c);
+  if (rc) return rc;
+  ctx_record_perf(c);
+  float pro = 0.f, att = 0.f;
+  cudaEventElapsedTime(&pro, c->ev[1], c->ev[4]);
+  cudaEventElapsedTime(&att, c->ev[4], c->ev[2]);
+  c->layer_prologue_ns = (uint64_t)llround((double)pro * 1e6);
+  c->layer_attention_ns = (uint64_t)llround((double)att * 1e6);
+  return LARA_OK;
+}
+
+int lara_read_layer_perf(lara_ctx* c, uint64_t* prologue_ns, uint64_t* attention_ns) {
+  int rc = ctx_check(c);
+  if (rc) return rc;
+  if (!prologue_ns || !attention_ns) return fail(LARA_ERR_STREAM_DEST, "null pointer");
+  *prologue_ns = c->layer_prologue_ns;
+  *attention_ns = c->layer_attention_ns;
   return LARA_OK;
 }
 

@@ -128,6 +128,9 @@ METHODS = {
                       "timeout_ms"],
     "read_perf": [], "save_last_profile": ["path"], "close": [], "status": [], "start": [], "clear_status": [],
     "byte_counts": ["seq_len"], "readback_o": ["seq_len", "out_buf"],
+    # sw/attn_driver.py:552-554
+    "run_layer": ["hidden_states", "wq", "wk", "wv", "rms_weight", "q_pos_base", "kv_pos_base", "causal",
+                  "timeout_ms"],
 }
 
 

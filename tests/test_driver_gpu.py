@@ -216,3 +216,37 @@ def test_run_query_pinned_host_buffers_match_pageable():
         assert 0 <= perf["mac_cycles"] <= perf["cycles"]
     gold = oracle.decode_attention(q, k, v, np.array([700, 1, 350]))
     assert_bf16_parity(o_pinned, gold, what="pinned run_query")
+
+
+def test_run_layer_composes_prologue_and_attention():
+    """run_layer (sw/attn_driver.py:552-586) = the GPU prologue followed by
+    run_attention on its q/k/v: the words match that composition exactly, the
+    result has the reference's [L, Hq*D] float32 layout, and the prologue
+    meets the oracle's tolerance."""
+    from lara_b200 import ops
+    from lara_b200.attn_driver import AttentionAccelerator
+    from oracle import prologue
+
+    rng = np.random.default_rng(21)
+    L, hidden = 96, 512
+    x = rng.standard_normal((L, hidden)).astype(np.float32)
+    wq = (rng.standard_normal((hidden, 32 * 128)) / np.sqrt(hidden)).astype(np.float32)
+    wk = (rng.standard_normal((hidden, 8 * 128)) / np.sqrt(hidden)).astype(np.float32)
+    wv = (rng.standard_normal((hidden, 8 * 128)) / np.sqrt(hidden)).astype(np.float32)
+    g = (1.0 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
+    pk = oracle.fp32_to_bf16_u16
+    with AttentionAccelerator() as acc:
+        out = acc.run_layer(x, wq, wk, wv, g, q_pos_base=31, kv_pos_base=7, causal=True)
+        prof = acc.last_profile
+        assert out.shape == (L, 32 * 128) and out.dtype == np.float32
+        assert prof.host_qkv_projection_ms > 0 and prof.layer_total_ms >= prof.host_qkv_projection_ms
+        dev = torch.device("cuda:0")
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(dev)  # noqa: E731
+        w_qkv = np.concatenate([pk(wq), pk(wk), pk(wv)], axis=1)
+        q, k, v = ops.layer_prologue(t(pk(x)), t(w_qkv), t(pk(g)), q_pos_base=31, kv_pos_base=7)
+        qw, kw, vw = words_of(q), words_of(k), words_of(v)
+        ref_words = acc.run_attention(qw, kw, vw, seq_len=L, q_pos_base=31, kv_pos_base=7, causal=True)
+    np.testing.assert_array_equal(out, oracle.bf16_u16_to_fp32(ref_words).transpose(1, 0, 2).reshape(L, 32 * 128))
+    gq, gk, gv = prologue.layer_prologue(pk(x), w_qkv, pk(g), q_pos_base=31, kv_pos_base=7)
+    assert_bf16_parity(qw, gq, what="run_layer q")
+    assert_bf16_parity(vw, gv, what="run_layer v")
