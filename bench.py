@@ -68,6 +68,9 @@ def parse_args():
     ap.add_argument("--seq-len", type=int, default=None)
     ap.add_argument("--splits", type=int, default=0, help="force the split count (0 = planner)")
     ap.add_argument("--chunk", type=int, default=0)
+    ap.add_argument("--paged", type=int, default=0, metavar="PAGE_SIZE",
+                    help="configs 2/3: decode from a paged cache (page pool in shuffled page order, block "
+                         "table) instead of the contiguous cache; 0 = contiguous")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
@@ -319,6 +322,48 @@ def _setup_decode(args, cfg, rank, world, dev):
         def step():
             dec(q, k, v, lens, out=o)
         launches = 3  # partial decode, NCCL all-gather, combine
+    elif args.paged:
+        import math
+
+        from lara_b200 import _native
+
+        dec = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, L, dev, lens=lens_np,
+                          num_splits=args.splits, chunk_tokens=args.chunk)
+        plan = dec.plan
+        ps = int(args.paged)
+        pps = math.ceil(L / ps)
+        npg = [math.ceil(int(n) / ps) for n in lens_np]
+        total = sum(npg)
+        perm = torch.randperm(total, generator=torch.Generator().manual_seed(7)).to(dev)
+        table = torch.full((B, pps), -1, dtype=torch.int32, device=dev)
+        kp = torch.empty((total, cfg.n_kv_heads, ps, cfg.head_dim), dtype=k.dtype, device=dev)
+        vp = torch.empty_like(kp)
+        base = 0
+        for b in range(B):
+            n = npg[b]
+            if n == 0:
+                continue
+            pages = perm[base:base + n]
+            table[b, :n] = pages.to(torch.int32)
+            for src, dst in ((k, kp), (v, vp)):
+                rows = src[b, :, : n * ps] if n * ps <= L else torch.nn.functional.pad(src[b], (0, 0, 0, n * ps - L))
+                dst.index_copy_(0, pages, rows.reshape(cfg.n_kv_heads, n, ps, cfg.head_dim).permute(1, 0, 2, 3))
+            base += n
+        del k, v
+        torch.cuda.empty_cache()
+        k, v = kp, vp
+        stream = torch.cuda.current_stream(dev)
+        scale = 1.0 / math.sqrt(cfg.head_dim)
+
+        def step():
+            _native.check(_native.lib.lara_gqa_decode_paged(
+                q.data_ptr(), kp.data_ptr(), vp.data_ptr(), table.data_ptr(), lens.data_ptr(), o.data_ptr(), B,
+                cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, ps, pps, total, scale, plan.num_splits,
+                plan.chunk_tokens, dec.workspace.data_ptr(), dec.workspace.numel(), stream.cuda_stream),
+                "decode_paged")
+        launches = 1
+        info["paged"] = {"page_size": ps, "pages": total, "page_order": "random permutation (seed 7)",
+                         "layout": "[pages][Hkv][page_size][D]"}
     else:
         dec = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, L, dev, lens=lens_np,
                           num_splits=args.splits, chunk_tokens=args.chunk)
@@ -391,7 +436,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         qn = q_host.numpy().view(np.uint16)
         on = o_host.numpy().view(np.uint16)
         e2e_steps = max(10, args.steps // 4)
-        if world == 1 or cfg.name != "long_context_splitkv":
+        if (world == 1 or cfg.name != "long_context_splitkv") and not args.paged:
             import ctypes
 
             from lara_b200 import _native
@@ -427,7 +472,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
                 e2e_step()
             e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
             barrier()
-            e2e_api = "lara_b200.parallel.SplitKVDecoder with pinned host q/o copies"
+            e2e_api = ("lara_gqa_decode_paged with pinned host q/o copies" if args.paged else
+                       "lara_b200.parallel.SplitKVDecoder with pinned host q/o copies")
         h2d, d2h = qn.nbytes, on.nbytes
         if not np.array_equal(on, o.view(torch.int16).cpu().numpy().view(np.uint16)):
             raise RuntimeError("API output differs from the timed kernel output")
@@ -447,7 +493,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     peak, peak_kind = measured_peak()
     value = total_bytes / (ms * 1e-3) / 1e9
     achieved = nbytes / (ms * 1e-3) / 1e9  # this GPU's bytes over the step
-    traffic = profiled_traffic() if cfg.name == "llama3_8b_decode" else None
+    traffic = profiled_traffic() if cfg.name == "llama3_8b_decode" and not args.paged else None
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()

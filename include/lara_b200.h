@@ -201,6 +201,37 @@ LARA_API int lara_attention_dense_board(const uint16_t* q, const uint16_t* k, co
                                         int n_q_heads, int n_kv_heads, int head_dim, int seq_len, int causal,
                                         int q_pos_base, int kv_pos_base, void* stream);
 
+/* Paged KV cache: K/V live in page pools k_pages/v_pages
+ * [num_pages][Hkv][page_size][D] (bf16; the rows of one (page, kv head) are
+ * contiguous) and block_table[b * pages_per_seq + j] (device int32) names the
+ * page holding tokens j*page_size .. (j+1)*page_size-1 of sequence b.  Pages
+ * may be shared between sequences (a common prefix) and appear in any order.
+ * page_size is a power of two in [16, 65536]; a sequence holds at most
+ * pages_per_seq * page_size tokens, which is the max_seq_len of
+ * lara_decode_plan / lara_decode_workspace_bytes.  A block-table entry outside
+ * [0, num_pages) is reported through the workspace status word (the access
+ * reads page 0 instead).  Otherwise identical to lara_gqa_decode: same
+ * arithmetic, same results bit for bit as a contiguous cache holding the
+ * same tokens.  (The reference keeps one sequence per transaction in BRAM,
+ * hw/rtl/mem/kv_cache_ram.sv; there is no counterpart of a page pool.) */
+LARA_API int lara_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pages, const uint16_t* v_pages,
+                                   const int32_t* block_table, const int32_t* seq_lens, uint16_t* o, int batch,
+                                   int n_q_heads, int n_kv_heads, int head_dim, int page_size, int pages_per_seq,
+                                   int num_pages, float scale, int num_splits, int chunk_tokens, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* Append n_new tokens per sequence (k/v_new[B][Hkv][n_new][D]) into a paged
+ * cache at positions seq_lens[b] .. seq_lens[b]+n_new-1, then advance
+ * seq_lens.  The pages those positions fall in must already be in the block
+ * table (the caller's page allocator assigns them).  Rows past the capacity or
+ * naming a bad page are dropped and flagged in the workspace status word
+ * (workspace may be NULL: no status).  Replaces: the K/V cache write of
+ * hw/rtl/mem/kv_cache_ram.sv:45-91 for a paged cache. */
+LARA_API int lara_kv_append_paged(uint16_t* k_pages, uint16_t* v_pages, const int32_t* block_table,
+                                  int32_t* seq_lens, const uint16_t* k_new, const uint16_t* v_new, int batch,
+                                  int n_kv_heads, int head_dim, int page_size, int pages_per_seq, int num_pages,
+                                  int n_new, void* workspace, void* stream);
+
 /* Layer prologue: the host half of AttentionAccelerator.run_layer
  * (sw/attn_driver.py:552-586) on the GPU, writing the run_attention layout.
  *   x_n = rms_weight ? bf16(fp32(fp32(x * inv) * rms_weight)) : x, with
@@ -306,6 +337,13 @@ LARA_API int lara_kv_append_ctx(lara_ctx* ctx, const uint16_t* k_new, const uint
  * lara_gqa_prefill); synchronous. */
 LARA_API int lara_run_prefill_chunk(lara_ctx* ctx, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
                                     uint16_t* o, int n_new, int causal, int on_device);
+
+/* Read the cache back: the first dst_len tokens of every (sequence, kv head)
+ * row into k/v[B][Hkv][dst_len][D] and the lengths into lens_out (host
+ * int32[B]); synchronous.  With lara_kv_load this saves and restores a cache
+ * (AttentionAccelerator.save_kv / restore_kv).  No reference counterpart: the
+ * FPGA's BRAM cache does not outlive a transaction. */
+LARA_API int lara_kv_read(lara_ctx* ctx, uint16_t* k, uint16_t* v, int32_t* lens_out, int dst_len, int on_device);
 
 /* Copy the current lengths (host int32[B]). */
 LARA_API int lara_get_seq_lens(lara_ctx* ctx, int32_t* lens_out);

@@ -97,6 +97,11 @@ SIGNATURES = {
                                      c_int, c_int, c_float, c_void_p, c_size_t, c_void_p]),
     "lara_attention_dense_board": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                            c_int, c_int, c_int, c_void_p]),
+    "lara_gqa_decode_paged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                      c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_size_t,
+                                      c_void_p]),
+    "lara_kv_append_paged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                     c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "lara_layer_prologue_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "lara_layer_prologue": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                     c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_void_p, c_size_t,
@@ -109,6 +114,7 @@ SIGNATURES = {
     "lara_kv_append_ctx": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lara_run_prefill_chunk": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
     "lara_get_seq_lens": (c_int, [c_void_p, c_void_p]),
+    "lara_kv_read": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lara_run_query": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
     "lara_run_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int]),
     "lara_read_perf": (c_int, [c_void_p, POINTER(LaraPerf)]),

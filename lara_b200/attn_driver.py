@@ -521,6 +521,35 @@ class AttentionAccelerator:
         check(lib.lara_kv_load(self._ctx, _ptr(kw), _ptr(vw), _ptr(ln), L, 0), "load_kv")
         self._max_len = int(ln.max()) if ln.size else 0
 
+    def save_kv(self, path) -> None:
+        """Write the resident cache to ``path`` (the ``lara-kv-v1`` format of
+        :mod:`lara_b200.kvfile`: lengths and the first max(len) tokens of every
+        (sequence, kv head) row as bf16 words)."""
+        from . import kvfile
+
+        self._require_open()
+        lens = self.seq_lens
+        n = max(int(lens.max()) if lens.size else 0, 1)
+        shape = (self.batch, self.n_kv_heads, n, self.head_dim)
+        k = np.empty(shape, np.uint16)
+        v = np.empty(shape, np.uint16)
+        check(lib.lara_kv_read(self._ctx, _ptr(k), _ptr(v), _ptr(lens), n, 0), "kv_read")
+        kvfile.save(path, k, v, lens)
+
+    def restore_kv(self, path) -> None:
+        """Load a cache written by :meth:`save_kv` (same batch, kv heads and
+        head_dim as this context; lengths must fit max_seq_len)."""
+        from . import kvfile
+
+        self._require_open()
+        k, v, lens = kvfile.load(path)
+        if k.shape[0] != self.batch or k.shape[1] != self.n_kv_heads or k.shape[3] != self.head_dim:
+            raise ValueError(f"{path}: cache geometry {k.shape} does not match batch={self.batch}, "
+                             f"n_kv_heads={self.n_kv_heads}, head_dim={self.head_dim}")
+        if k.shape[2] > self.max_seq_len:
+            raise ValueError(f"{path}: {k.shape[2]} tokens exceed max_seq_len={self.max_seq_len}")
+        self.load_kv(k, v, lens)
+
     def append_kv(self, k_new: np.ndarray, v_new: np.ndarray) -> None:
         """Append ``k/v_new[B, Hkv, n, D]`` (or ``[B, Hkv, D]`` for one token)."""
         self._require_open()

@@ -87,7 +87,8 @@ int resolve_plan(int batch, int hq, int hkv, int d, int lmax, const int32_t* len
 
 int decode_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int32_t* lens, uint16_t* o,
                   float* out_ml, float* out_acc, int batch, int hq, int hkv, int d, int lmax, float scale, int nsplit,
-                  int chunk, void* ws, size_t ws_bytes, void* stream) {
+                  int chunk, void* ws, size_t ws_bytes, void* stream, const int32_t* block_table = nullptr,
+                  int page_log2 = 0, int pages_per_seq = 0, int num_pages = 0) {
   int rc = check_geometry(batch, hq, hkv, d, lmax);
   if (rc) return rc;
   if (!q || !k || !v || !lens || !ws || (!o && !out_acc))
@@ -115,8 +116,22 @@ int decode_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, const
   p.part_ml = reinterpret_cast<float*>(base + w.ml_off);
   p.part_acc = reinterpret_cast<float*>(base + w.acc_off);
   p.out_ml = out_ml; p.out_acc = out_acc;
+  p.block_table = block_table; p.page_log2 = page_log2; p.pages_per_seq = pages_per_seq; p.num_pages = num_pages;
   cudaError_t e = lara::decode_launch(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return LARA_OK;
+}
+
+// Paged-cache geometry: page a power of two in [16, 65536], and the per
+// sequence capacity pages_per_seq * page_size representable as int.
+int check_paged(int page_size, int pages_per_seq, int num_pages, int* page_log2) {
+  if (page_size < 16 || page_size > 65536 || (page_size & (page_size - 1)))
+    return fail(LARA_ERR_BAD_CFG, "page_size must be a power of two in [16, 65536], got %d", page_size);
+  if (pages_per_seq < 1 || num_pages < 1 || (long long)pages_per_seq * page_size > 0x7fffffffll)
+    return fail(LARA_ERR_BAD_CFG, "bad paged-cache geometry");
+  int l = 0;
+  while ((1 << l) < page_size) ++l;
+  *page_log2 = l;
   return LARA_OK;
 }
 
@@ -275,6 +290,7 @@ std::string describe_status(int bits) {
   if (bits & lara::kDevWaitTimeout) s += " wait-timeout";
   if (bits & lara::kDevBadLength) s += " bad-sequence-length";
   if (bits & lara::kDevAppendOverflow) s += " append-overflow";
+  if (bits & lara::kDevBadPage) s += " bad-page-index";
   return s.empty() ? std::string(" unknown") : s;
 }
 
@@ -403,6 +419,39 @@ int lara_kv_append(uint16_t* k_cache, uint16_t* v_cache, int32_t* seq_lens, cons
   cudaError_t e = lara::kv_append_launch(k_cache, v_cache, seq_lens, k_new, v_new, batch, n_kv_heads, head_dim,
                                          max_seq_len, n_new, status, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+  return LARA_OK;
+}
+
+int lara_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pages, const uint16_t* v_pages,
+                          const int32_t* block_table, const int32_t* seq_lens, uint16_t* o, int batch, int n_q_heads,
+                          int n_kv_heads, int head_dim, int page_size, int pages_per_seq, int num_pages, float scale,
+                          int num_splits, int chunk_tokens, void* workspace, size_t workspace_bytes, void* stream) {
+  int page_log2 = 0;
+  int rc = check_paged(page_size, pages_per_seq, num_pages, &page_log2);
+  if (rc) return rc;
+  if (!block_table) return fail(LARA_ERR_STREAM_DEST, "null block table");
+  return decode_common(q, k_pages, v_pages, seq_lens, o, nullptr, nullptr, batch, n_q_heads, n_kv_heads, head_dim,
+                       pages_per_seq * page_size, scale, num_splits, chunk_tokens, workspace, workspace_bytes, stream,
+                       block_table, page_log2, pages_per_seq, num_pages);
+}
+
+int lara_kv_append_paged(uint16_t* k_pages, uint16_t* v_pages, const int32_t* block_table, int32_t* seq_lens,
+                         const uint16_t* k_new, const uint16_t* v_new, int batch, int n_kv_heads, int head_dim,
+                         int page_size, int pages_per_seq, int num_pages, int n_new, void* workspace, void* stream) {
+  if (!k_pages || !v_pages || !block_table || !seq_lens || !k_new || !v_new)
+    return fail(LARA_ERR_STREAM_DEST, "null pointer");
+  int page_log2 = 0;
+  int rc = check_paged(page_size, pages_per_seq, num_pages, &page_log2);
+  if (rc) return rc;
+  if (batch < 1 || n_kv_heads < 1 || head_dim < 8 || head_dim % 8 || n_new < 0)
+    return fail(LARA_ERR_BAD_CFG, "bad append geometry");
+  if (!aligned(k_pages, 16) || !aligned(v_pages, 16) || !aligned(k_new, 16) || !aligned(v_new, 16))
+    return fail(LARA_ERR_STREAM_DEST, "pages and new rows must be 16-byte aligned");
+  int* status = workspace ? static_cast<int*>(workspace) : nullptr;
+  cudaError_t e = lara::kv_append_paged_launch(k_pages, v_pages, block_table, seq_lens, k_new, v_new, batch,
+                                               n_kv_heads, head_dim, page_log2, pages_per_seq, num_pages, n_new,
+                                               status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "paged append launch");
   return LARA_OK;
 }
 
@@ -799,6 +848,25 @@ int lara_run_prefill_chunk(lara_ctx* c, const uint16_t* q, const uint16_t* k_new
   rc = ctx_finish(c);
   if (rc) return rc;
   ctx_record_perf(c);
+  return LARA_OK;
+}
+
+int lara_kv_read(lara_ctx* c, uint16_t* k, uint16_t* v, int32_t* lens_out, int dst_len, int on_device) {
+  int rc = ctx_check(c);
+  if (rc) return rc;
+  if (!k || !v || !lens_out) return fail(LARA_ERR_STREAM_DEST, "null pointer");
+  if (dst_len < 1 || dst_len > c->lmax) return fail(LARA_ERR_BAD_CFG, "dst_len must be in [1, max_seq_len]");
+  DeviceGuard g(c->device);
+  const size_t row = (size_t)c->d * 2;
+  const size_t rows = (size_t)c->batch * c->hkv;
+  const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+  // each (sequence, kv head) row: its first dst_len tokens
+  LARA_CUDA(cudaMemcpy2DAsync(k, (size_t)dst_len * row, c->k_cache, (size_t)c->lmax * row, (size_t)dst_len * row,
+                              rows, kind, c->stream));
+  LARA_CUDA(cudaMemcpy2DAsync(v, (size_t)dst_len * row, c->v_cache, (size_t)c->lmax * row, (size_t)dst_len * row,
+                              rows, kind, c->stream));
+  LARA_CUDA(cudaStreamSynchronize(c->stream));
+  for (int b = 0; b < c->batch; ++b) lens_out[b] = c->lens_host[b];
   return LARA_OK;
 }
 

@@ -44,6 +44,7 @@ namespace {
 constexpr int ilog2(int x) { return x <= 1 ? 0 : 1 + ilog2(x / 2); }
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
+constexpr int kPageCacheEntries = 256;  // block-table entries of a CTA's chunk kept in shared memory
 
 template <int D, int G>
 struct Traits {
@@ -76,7 +77,9 @@ struct Traits {
   static constexpr int kBarOff = (kCbufOff + kCbufFloats * 4 + 15) / 16 * 16;  // full[], empty[]
   static constexpr int kCntOff = kBarOff + 2 * kStages * 8;                      // refill round per stage
   static constexpr int kFlagOff = kCntOff + kStages * 4;
-  static constexpr int kSmemBytes = kFlagOff + 16;
+  static constexpr int kPageCache = kPageCacheEntries;
+  static constexpr int kPageOff = kFlagOff + 16;
+  static constexpr int kSmemBytes = kPageOff + kPageCache * 4;
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
   static_assert(kLPT <= 32 && 32 % kLPT == 0, "a token row must fit one warp");
   static_assert(G >= 1 && G <= kLPT && (G & (G - 1)) == 0, "group size must be a power of two <= lanes per row");
@@ -93,18 +96,47 @@ __device__ __forceinline__ int seq_len_of(const DecodeParams& p, int seq, int ro
   return len < 0 ? 0 : (len > p.max_seq_len ? p.max_seq_len : (int)len);
 }
 
+// Page of the token `tok` of `seq` (paged caches).  Entries of the CTA's chunk
+// are staged in shared memory; an out-of-range entry flags the status word and
+// reads page 0 instead, so every issued copy stays in bounds and completes.
+__device__ __forceinline__ int page_of(const DecodeParams& p, const int* pcache, int seq, int tok, int tok_begin) {
+  const int idx = (tok >> p.page_log2) - (tok_begin >> p.page_log2);
+  int page = idx < kPageCacheEntries ? pcache[idx] : __ldg(p.block_table + (long long)seq * p.pages_per_seq + (tok >> p.page_log2));
+  if (page < 0 || page >= p.num_pages) {
+    atomicOr(p.status, kDevBadPage);
+    page = 0;
+  }
+  return page;
+}
+
 // Issue the bulk copies of tile `t` (K rows then V rows) into stage `st`.
 template <int D, int G>
-__device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t, int ntok, const uint16_t* kg,
-                                           const uint16_t* vg, uint64_t pol) {
+__device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t, int ntok, const DecodeParams& p,
+                                           int seq, int kvh, int tok_begin, const int* pcache, uint64_t pol) {
   using T = Traits<D, G>;
   const int st = t % T::kStages;
   const int n = min(T::kTile, ntok - t * T::kTile);
   const uint32_t bytes = (uint32_t)n * T::kRowBytes;
   uint8_t* stage = smem + st * T::kStageBytes;
   mbar_arrive_expect_tx(&full[st], 2u * bytes);
-  bulk_g2s(stage, kg + (long long)t * T::kTile * D, bytes, &full[st], pol);
-  bulk_g2s(stage + T::kHalfStage, vg + (long long)t * T::kTile * D, bytes, &full[st], pol);
+  const int tok0 = tok_begin + t * T::kTile;
+  if (p.block_table == nullptr) {
+    const long long off = (long long)seq * p.kv_sb + (long long)kvh * p.kv_sh + (long long)tok0 * D;
+    bulk_g2s(stage, p.k + off, bytes, &full[st], pol);
+    bulk_g2s(stage + T::kHalfStage, p.v + off, bytes, &full[st], pol);
+    return;
+  }
+  // a tile may span several pages (page < tile) or lie inside one
+  const int ps = 1 << p.page_log2;
+  for (int r = 0; r < n;) {
+    const int tok = tok0 + r;
+    const int in_page = tok & (ps - 1);
+    const int cnt = min(n - r, ps - in_page);
+    const long long off = (((long long)page_of(p, pcache, seq, tok, tok_begin) * p.n_kv_heads + kvh) * ps + in_page) * D;
+    bulk_g2s(stage + r * T::kRowBytes, p.k + off, (uint32_t)cnt * T::kRowBytes, &full[st], pol);
+    bulk_g2s(stage + T::kHalfStage + r * T::kRowBytes, p.v + off, (uint32_t)cnt * T::kRowBytes, &full[st], pol);
+    r += cnt;
+  }
 }
 
 template <int D, int G>
@@ -155,10 +187,16 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   float* pbuf = reinterpret_cast<float*>(smem + T::kPbufOff);
   float* cbuf = reinterpret_cast<float*>(smem + T::kCbufOff);
 
-  const long long kv_base = (long long)seq * p.kv_sb + (long long)kvh * p.kv_sh + (long long)tok_begin * D;
-  const uint16_t* kg = p.k + kv_base;
-  const uint16_t* vg = p.v + kv_base;
   const uint64_t pol = make_evict_first_policy();
+  int* pcache = reinterpret_cast<int*>(smem + T::kPageOff);
+  if (p.block_table != nullptr) {
+    // block-table entries of this CTA's chunk (the first kPageCache of them)
+    const int first_page = tok_begin >> p.page_log2;
+    const int npages = min(T::kPageCache, ((tok_begin + ntok - 1) >> p.page_log2) - first_page + 1);
+    for (int i = threadIdx.x; i < npages; i += T::kThreads)
+      pcache[i] = __ldg(p.block_table + (long long)seq * p.pages_per_seq + first_page + i);
+    __syncthreads();
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < T::kStages; ++s) {
@@ -171,7 +209,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     flag[2] = 0;  // tiles issued
     mbar_fence_init();
     const int first = ntiles < T::kStages ? ntiles : T::kStages;
-    for (int t = 0; t < first; ++t) issue_tile<D, G>(smem, full, t, ntok, kg, vg, pol);
+    for (int t = 0; t < first; ++t) issue_tile<D, G>(smem, full, t, ntok, p, seq, kvh, tok_begin, pcache, pol);
     flag[2] = first;
   }
   __syncthreads();
@@ -317,7 +355,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
       const int nxt = i + T::kStages;
       if (nxt < ntiles && mbar_test_wait(&empty[st], round & 1) &&
           atomicCAS(&refill_round[st], round, round + 1) == round) {
-        issue_tile<D, G>(smem, full, nxt, ntok, kg, vg, pol);
+        issue_tile<D, G>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pcache, pol);
         atomicMax(&flag[2], nxt + 1);
       }
     }

@@ -4,6 +4,8 @@
 //   hw/rtl/mem/kv_cache_ram.sv:45-91 (write address token*128+dim): new
 //   rows land at position lens[b] of each (sequence, kv head) row of the HBM
 //   cache [B, Hkv, Lmax, D]; lens[b] then advances by n_new.
+// * kv_append_paged: the same write into a paged cache (page pool plus a
+//   per-sequence block table).
 // * pack_bf16: the reference's host packer fp32_to_bf16_u16
 //   (sw/attn_driver.py:88-98) as a device kernel with the same integer steps.
 // * lse_combine: merges P partial results (m in log2 domain, l, unnormalised
@@ -42,6 +44,42 @@ __global__ void kv_append_kernel(uint16_t* __restrict__ k_cache, uint16_t* __res
     const long long src = row * head_dim + vec * 8;
     *reinterpret_cast<uint4*>(k_cache + dst) = *reinterpret_cast<const uint4*>(k_new + src);
     *reinterpret_cast<uint4*>(v_cache + dst) = *reinterpret_cast<const uint4*>(v_new + src);
+  }
+}
+
+// Paged cache: row (b, h, t) lands in page block_table[b][pos >> page_log2],
+// row pos & (page - 1), pos = lens[b] + t, of the pool [pages][Hkv][page][D].
+__global__ void kv_append_paged_kernel(uint16_t* __restrict__ k_pages, uint16_t* __restrict__ v_pages,
+                                       const int32_t* __restrict__ block_table, const int32_t* __restrict__ lens,
+                                       const uint16_t* __restrict__ k_new, const uint16_t* __restrict__ v_new,
+                                       int batch, int n_kv_heads, int head_dim, int page_log2, int pages_per_seq,
+                                       int num_pages, int n_new, int* status) {
+  const int vec_per_row = head_dim / 8;
+  const long long max_seq_len = (long long)pages_per_seq << page_log2;
+  const long long total = (long long)batch * n_kv_heads * n_new * vec_per_row;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / vec_per_row;
+    const int vec = (int)(i % vec_per_row);
+    const int t = (int)(row % n_new);
+    const long long bh = row / n_new;
+    const int b = (int)(bh / n_kv_heads), h = (int)(bh % n_kv_heads);
+    const int len = lens[b];
+    const long long pos = (long long)len + t;
+    if (len < 0 || pos >= max_seq_len) {
+      if (status) atomicOr(status, kDevAppendOverflow);
+      continue;
+    }
+    const int page = block_table[(long long)b * pages_per_seq + (pos >> page_log2)];
+    if (page < 0 || page >= num_pages) {
+      if (status) atomicOr(status, kDevBadPage);
+      continue;
+    }
+    const long long in_page = pos & ((1ll << page_log2) - 1);
+    const long long dst = ((((long long)page * n_kv_heads + h) << page_log2) + in_page) * head_dim + vec * 8;
+    const long long src = row * head_dim + vec * 8;
+    *reinterpret_cast<uint4*>(k_pages + dst) = *reinterpret_cast<const uint4*>(k_new + src);
+    *reinterpret_cast<uint4*>(v_pages + dst) = *reinterpret_cast<const uint4*>(v_new + src);
   }
 }
 
@@ -127,6 +165,22 @@ cudaError_t kv_append_launch(uint16_t* k_cache, uint16_t* v_cache, int32_t* lens
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   lens_add_kernel<<<(batch + 255) / 256, 256, 0, stream>>>(lens, batch, n_new, max_seq_len);
+  return cudaGetLastError();
+}
+
+cudaError_t kv_append_paged_launch(uint16_t* k_pages, uint16_t* v_pages, const int32_t* block_table, int32_t* lens,
+                                   const uint16_t* k_new, const uint16_t* v_new, int batch, int n_kv_heads,
+                                   int head_dim, int page_log2, int pages_per_seq, int num_pages, int n_new,
+                                   int* status, cudaStream_t stream) {
+  if (n_new <= 0) return cudaSuccess;
+  const long long work = (long long)batch * n_kv_heads * n_new * (head_dim / 8);
+  kv_append_paged_kernel<<<grid_for(work, 256), 256, 0, stream>>>(k_pages, v_pages, block_table, lens, k_new, v_new,
+                                                                 batch, n_kv_heads, head_dim, page_log2,
+                                                                 pages_per_seq, num_pages, n_new, status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const long long cap = (long long)pages_per_seq << page_log2;
+  lens_add_kernel<<<(batch + 255) / 256, 256, 0, stream>>>(lens, batch, n_new, (int)(cap > 0x7fffffff ? 0x7fffffff : cap));
   return cudaGetLastError();
 }
 

@@ -16,6 +16,7 @@ enum DeviceStatus : int {
   kDevWaitTimeout = 1 << 0,    // a bounded mbarrier wait gave up
   kDevBadLength = 1 << 1,      // a sequence length was outside [0, max_seq_len]
   kDevAppendOverflow = 1 << 2, // an appended row would pass max_seq_len
+  kDevBadPage = 1 << 3,        // a block-table entry was outside [0, num_pages)
 };
 
 // One decode launch: queries of `batch` sequences (or of `batch` query rows
@@ -55,6 +56,12 @@ struct DecodeParams {
   // instead of bf16 output.
   float* out_ml;       // [batch * n_q_heads * 2]
   float* out_acc;      // [batch * n_q_heads * head_dim]
+  // Paged cache (when block_table != nullptr): k/v are page pools
+  // [num_pages][n_kv_heads][1 << page_log2][head_dim]; token t of sequence s
+  // lives in page block_table[s * pages_per_seq + (t >> page_log2)] at row
+  // t & ((1 << page_log2) - 1); kv_sb / kv_sh are unused.
+  const int32_t* block_table;
+  int page_log2, pages_per_seq, num_pages;
 };
 
 struct WorkspaceLayout {
@@ -111,6 +118,10 @@ cudaError_t kv_append_launch(uint16_t* k_cache, uint16_t* v_cache, int32_t* lens
                              const uint16_t* v_new, int batch, int n_kv_heads, int head_dim, int max_seq_len,
                              int n_new, int* status, cudaStream_t stream);
 
+cudaError_t kv_append_paged_launch(uint16_t* k_pages, uint16_t* v_pages, const int32_t* block_table, int32_t* lens,
+                                   const uint16_t* k_new, const uint16_t* v_new, int batch, int n_kv_heads,
+                                   int head_dim, int page_log2, int pages_per_seq, int num_pages, int n_new,
+                                   int* status, cudaStream_t stream);
 cudaError_t pack_bf16_launch(const float* src, uint16_t* dst, size_t n, cudaStream_t stream);
 
 int device_sm_count();
