@@ -1,33 +1,33 @@
 // Chunked prefill / dense attention on the 5th-generation tensor cores
 // (tcgen05 + TMEM, sm_100a).
 //
-// One CTA computes 128 query rows of one query head of one sequence against
-// the visible prefix of its KV cache ("cache + self" with the causal rule
-// kv_pos <= q_pos of sw/board_performance.py:174-177), FlashAttention-style:
+// One CTA computes two tiles of 128 query rows (A: q0 .. q0+127, B: q0+128 ..
+// q0+255) of one query head of one sequence against the visible prefix of its
+// KV cache ("cache + self" with the causal rule kv_pos <= q_pos of
+// sw/board_performance.py:174-177), FlashAttention-style, with the two tiles
+// in ping-pong so the tensor core works on one while the other's softmax runs:
 //
-//   warp 5 (TMA)     : Q tile once, then K_j / V_j tiles of 128 keys into a
-//                      2-stage ring (tensor-map copies with 128-byte swizzle,
-//                      no multicast), mbarrier transaction counts.
-//   warp 4 (MMA)     : one thread issues tcgen05.mma:
-//                        S_j = Q . K_j^T   (A, B from shared memory, fp32 in TMEM,
-//                                           double-buffered S so S_{j+1} overlaps
-//                                           the softmax of S_j)
-//                        O  += P_j . V_j   (A = P_j read from TMEM, B = V_j MN-major)
-//                      and tcgen05.commit to mbarriers.
-//   warps 0-7        : two threads per query row (TMEM lane), one per half of
-//                      the 128 columns: load S_j, scale,
-//                      causal/length mask, online softmax in log2 domain (fp32
-//                      running max and sum; the pair exchanges row maxima
-//                      through shared memory), P_j -> bf16 (round to nearest
-//                      even) written back into the S buffer for the P.V MMA,
-//                      rescale of the O accumulator in TMEM when the
-//                      reference max moved, and the epilogue O / l -> bf16.
+//   warp 9 (TMA)     : Q_A and Q_B once, then K_j / V_j tiles of 128 keys into
+//                      a 2-stage ring (tensor-map copies with 128-byte
+//                      swizzle, no multicast), mbarrier transaction counts.
+//   warp 8 (MMA)     : one thread issues tcgen05.mma in the order
+//                      PV_A(j), S_A(j+1), PV_B(j), S_B(j+1):
+//                        S_t = Q_t . K^T   (A, B from shared memory, fp32 in TMEM)
+//                        O_t += P_t . V    (A = P_t read from TMEM, B = V MN-major)
+//                      and tcgen05.commit to mbarriers.  TMEM: S_A | S_B | O_A | O_B.
+//   warps 0-3 / 4-7  : softmax of tile A / B, one thread per query row (TMEM
+//                      lane) holding its 128 scores: scale, causal/length mask,
+//                      online softmax in log2 domain (fp32 running max and
+//                      sum), P -> bf16 (round to nearest even; by default split
+//                      into P_hi + P_lo for ~16 significant bits) written back
+//                      into the S columns for the P.V MMA, rescale of O_t in
+//                      TMEM when the reference max moved, epilogue O_t / l -> bf16.
 //
-// KV tiles beyond the last key visible to any row of the tile are never
-// loaded (the causal tile skip of hw/rtl/core/attn_core.sv:138-153); the
-// diagonal tile is masked per element.  Every wait is bounded by
-// %globaltimer; on a timeout the CTA flags the status word, drains its own
-// tensor-core work and TMA copies (bounded), frees TMEM and returns.
+// KV tiles beyond the last key visible to any row of the CTA are never loaded
+// (the causal tile skip of hw/rtl/core/attn_core.sv:138-153); the diagonal
+// tiles are masked per element.  Every wait is bounded by %globaltimer; on a
+// timeout the CTA flags the status word, drains its own tensor-core work and
+// TMA copies (bounded), frees TMEM and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -50,38 +50,10 @@ constexpr int kTileN = 128;        // keys per KV tile
 constexpr int kHead = 128;         // head_dim
 constexpr int kHalfBytes = 128 * 128;  // one [128 rows x 64 bf16] swizzled half tile
 constexpr int kTileBytes = 2 * kHalfBytes;  // [128 x 128] bf16 as two halves
-constexpr int kStages = 2;
-constexpr int kSoftmaxWarps = 8;   // two per TMEM lane quarter: each owns 64 of a row's 128 columns
-constexpr int kMmaWarp = kSoftmaxWarps;
-constexpr int kTmaWarp = kSoftmaxWarps + 1;
-constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
 // The reference max used for exponentiation only moves when a row's max grows
 // by more than this (log2 units), so O is rarely rescaled; p stays <= 2^8.
 constexpr float kRescaleThreshold = 8.0f;
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
-
-// shared memory map (offsets from a 1024-aligned base)
-constexpr int kQOff = 0;
-constexpr int kKOff = kQOff + kTileBytes;                 // K stages
-constexpr int kVOff = kKOff + kStages * kTileBytes;       // V stages
-constexpr int kBarOff = kVOff + kStages * kTileBytes;
-constexpr int kRedOff = kBarOff + 256;                    // row-max / row-sum exchange [2][2][128] floats
-constexpr int kSmemUsed = kRedOff + 2 * 2 * kTileM * 4;
-constexpr int kSmemAlloc = kSmemUsed + 1024;  // + alignment slack
-
-struct Bars {
-  uint64_t q_full;
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t o_full;
-  uint64_t drain;
-  uint32_t tmem_base;
-  int abort;
-  int issued;  // KV tiles whose TMA copies were issued
-};
-static_assert(sizeof(Bars) <= 256, "barrier block");
+constexpr uint32_t kTmemCols = 512;  // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
 
 struct TcArgs {
   int n_q;            // query rows per sequence
@@ -98,39 +70,65 @@ struct TcArgs {
   int* status;
 };
 
-// kSplitP: P = P_hi + P_lo (two bf16 terms, ~16 significant bits) and two
-// P.V MMA sets, so the result carries fp32-class P precision; without it P is
-// one bf16 (the usual FlashAttention choice).
+// ---------------------------------------------------------------------------
+// Two query tiles per CTA ("ping-pong"): rows q0 .. q0+127 (tile A) and
+// q0+128 .. q0+255 (tile B) of one head share every K/V tile.  TMEM holds
+// S_A | S_B | O_A | O_B (128 columns each).  The MMA thread interleaves the
+// tiles -- PV_A(j), S_A(j+1), PV_B(j), S_B(j+1) -- so the tensor core works
+// on one tile while the other tile's softmax runs.  Softmax: warps 0-3 own
+// tile A, warps 4-7 tile B, one thread per query row holding its 128 scores.
+// ---------------------------------------------------------------------------
+constexpr int kPPStages = 2;
+constexpr int kPPQOff = 0;                                  // Q_A, then Q_B
+constexpr int kPPKOff = 2 * kTileBytes;
+constexpr int kPPVOff = kPPKOff + kPPStages * kTileBytes;
+constexpr int kPPBarOff = kPPVOff + kPPStages * kTileBytes;
+constexpr int kPPSmemAlloc = kPPBarOff + 256 + 1024;
+constexpr int kPPMmaWarp = 8;
+constexpr int kPPTmaWarp = 9;
+constexpr int kPPThreads = 10 * 32;
+
+struct PPBars {
+  uint64_t q_full;
+  uint64_t kv_full[kPPStages];
+  uint64_t kv_empty[kPPStages];
+  uint64_t s_full[2];  // per tile
+  uint64_t p_full[2];  // per tile: 128 softmax threads
+  uint64_t o_full[2];  // per tile
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int issued;
+};
+static_assert(sizeof(PPBars) <= 256, "barrier block");
+
 template <bool kSplitP>
-__global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+__global__ void __launch_bounds__(kPPThreads, 1)
+    prefill_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(smem + kBarOff);
+  PPBars* bars = reinterpret_cast<PPBars*>(smem + kPPBarOff);
   volatile int* abort = &bars->abort;
 
   const int h = blockIdx.x;
-  const int qt = blockIdx.y;
   const int b = blockIdx.z;
   const int kvh = h / (a.n_q_heads / a.n_kv_heads);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q0 = qt * kTileM;
+  const int q0 = blockIdx.y * 2 * kTileM;
 
-  // visible keys of this tile: rows q0 .. q_last see keys [0, min(kv_len, q_off + row + 1))
   const int base = a.base_lens ? a.base_lens[b] : 0;
   int kv_len = base + a.kv_add;
   kv_len = kv_len < 0 ? 0 : (kv_len > a.kv_rows ? a.kv_rows : kv_len);
   const int q_off = base + a.q_add;
-  const int q_last = min(a.n_q, q0 + kTileM) - 1;
+  const int q_last = min(a.n_q, q0 + 2 * kTileM) - 1;
   long long kmax = (long long)kv_len - 1;
   if (a.causal) kmax = min(kmax, (long long)q_off + q_last);
   const int ntiles = kmax >= 0 ? (int)(kmax / kTileN) + 1 : 0;
 
   if (ntiles == 0) {
-    // no row of this tile sees any key: zero output (l == 0 -> 0)
-    if (threadIdx.x < kTileM) {
+    if (threadIdx.x < 2 * kTileM) {
       const int r = q0 + threadIdx.x;
       if (r < a.n_q) {
         uint16_t* dst = a.o + b * a.o_sb + (long long)r * a.o_sr + (long long)h * a.o_sh;
@@ -140,23 +138,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
 
-  uint8_t* q_smem = smem + kQOff;
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kPPStages; ++s) {
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
     }
-    mbar_init(&bars->s_full[0], 1);
-    mbar_init(&bars->s_full[1], 1);
-    mbar_init(&bars->p_full, kSoftmaxWarps * 32);
-    mbar_init(&bars->o_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bars->s_full[t], 1);
+      mbar_init(&bars->p_full[t], kTileM);
+      mbar_init(&bars->o_full[t], 1);
+    }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
     bars->issued = 0;
     mbar_fence_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == kPPMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&bars->tmem_base)),
                  "r"(kTmemCols)
                  : "memory");
@@ -166,20 +164,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t tm_o = tmem + 256;
 
-  if (warp == kTmaWarp) {
+  if (warp == kPPTmaWarp) {
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bars->q_full, kTileBytes);
-      tma_load_4d(q_smem, &tm_q, 0, h, q0, b, &bars->q_full);
-      tma_load_4d(q_smem + kHalfBytes, &tm_q, 64, h, q0, b, &bars->q_full);
+      uint8_t* q_smem = smem + kPPQOff;
+      mbar_arrive_expect_tx(&bars->q_full, 2 * kTileBytes);
+      for (int t = 0; t < 2; ++t) {
+        tma_load_4d(q_smem + t * kTileBytes, &tm_q, 0, h, q0 + t * kTileM, b, &bars->q_full);
+        tma_load_4d(q_smem + t * kTileBytes + kHalfBytes, &tm_q, 64, h, q0 + t * kTileM, b, &bars->q_full);
+      }
       const int zrow = b * a.n_kv_heads + kvh;
       for (int j = 0; j < ntiles; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages && !wait_or_abort(&bars->kv_empty[st], ((j / kStages) - 1) & 1, abort)) break;
-        uint8_t* ks = smem + kKOff + st * kTileBytes;
-        uint8_t* vs = smem + kVOff + st * kTileBytes;
+        const int st = j % kPPStages;
+        if (j >= kPPStages && !wait_or_abort(&bars->kv_empty[st], ((j / kPPStages) - 1) & 1, abort)) break;
+        uint8_t* ks = smem + kPPKOff + st * kTileBytes;
+        uint8_t* vs = smem + kPPVOff + st * kTileBytes;
         mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kTileBytes);
         tma_load_3d(ks, &tm_k, 0, j * kTileN, zrow, &bars->kv_full[st]);
         tma_load_3d(ks + kHalfBytes, &tm_k, 64, j * kTileN, zrow, &bars->kv_full[st]);
@@ -188,160 +188,179 @@ __global__ void __launch_bounds__(kThreads, 1)
         bars->issued = j + 1;
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kPPMmaWarp) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       const uint32_t id_s = idesc_bf16(kTileM, kTileN, 0);
       const uint32_t id_pv = idesc_bf16(kTileM, kTileN, 1);
-      const uint32_t q_base = smem_addr(q_smem);
-      bool ok = wait_or_abort(&bars->q_full, 0, abort);
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int st = j % kStages;
-          const int sb = j & 1;
-          if (!wait_or_abort(&bars->kv_full[st], (j / kStages) & 1, abort)) break;
-          tc_fence_after();
-          const uint32_t k_base = smem_addr(smem + kKOff + st * kTileBytes);
-          // S_j = Q . K_j^T over head_dim in 8 steps of 16
+      const uint32_t q_base = smem_addr(smem + kPPQOff);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t k_base = smem_addr(smem + kPPKOff + (j % kPPStages) * kTileBytes);
+        const uint32_t qb = q_base + t * kTileBytes;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-            mma_ss(tmem + sb * 128, desc_sw128(q_base + off, 16, 1024), desc_sw128(k_base + off, 16, 1024), id_s,
-                   kk > 0);
-          }
-          mma_commit(&bars->s_full[sb]);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_ss(tmem + t * 128, desc_sw128(qb + off, 16, 1024), desc_sw128(k_base + off, 16, 1024), id_s, kk > 0);
         }
-        if (j >= 1) {
-          // O += P_{j-1} . V_{j-1} once the softmax has written P and rescaled O
-          const int jp = j - 1;
-          if (!wait_or_abort(&bars->p_full, jp & 1, abort)) break;
-          tc_fence_after();
-          const int st = jp % kStages;
-          const uint32_t v_base = smem_addr(smem + kVOff + st * kTileBytes);
-          const uint32_t p_tmem = tmem + (jp & 1) * 128;
+        mma_commit(&bars->s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_base = smem_addr(smem + kPPVOff + (j % kPPStages) * kTileBytes);
+        const uint32_t p_tmem = tmem + t * 128;
+        const uint32_t o_tmem = tmem + 256 + t * 128;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts(o_tmem, p_tmem + kk * 8, desc_sw128(v_base + kk * 16 * 128, kHalfBytes, 1024), id_pv,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        if constexpr (kSplitP) {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tm_o, p_tmem + kk * 8, desc_sw128(v_base + kk * 16 * 128, kHalfBytes, 1024), id_pv,
-                   (jp > 0 || kk > 0) ? 1u : 0u);
-          if constexpr (kSplitP) {
-            // low-order part of P, stored in columns 64..127 of the S buffer
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              mma_ts(tm_o, p_tmem + 64 + kk * 8, desc_sw128(v_base + kk * 16 * 128, kHalfBytes, 1024), id_pv, 1u);
-          }
-          mma_commit(&bars->o_full);
-          mma_commit(&bars->kv_empty[st]);
+            mma_ts(o_tmem, p_tmem + 64 + kk * 8, desc_sw128(v_base + kk * 16 * 128, kHalfBytes, 1024), id_pv, 1u);
         }
+        mma_commit(&bars->o_full[t]);
+      };
+      bool ok = wait_or_abort(&bars->q_full, 0, abort) && wait_or_abort(&bars->kv_full[0], 0, abort);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
       }
-      // drain: every tcgen05 op this thread issued is complete once `drain` fires
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const bool more = j + 1 < ntiles;
+        // tile A: PV_A(j), then S_A(j+1) (in-order issue keeps P_A(j) intact until PV_A(j) has read it)
+        if (!wait_or_abort(&bars->p_full[0], j & 1, abort)) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!wait_or_abort(&bars->kv_full[(j + 1) % kPPStages], ((j + 1) / kPPStages) & 1, abort)) break;
+          tc_fence_after();
+          issue_s(0, j + 1);
+        }
+        // tile B
+        if (!wait_or_abort(&bars->p_full[1], j & 1, abort)) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        mma_commit(&bars->kv_empty[j % kPPStages]);
+        if (more) issue_s(1, j + 1);
+      }
       mma_commit(&bars->drain);
       (void)mbar_wait_bounded(&bars->drain, 0);
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int quarter = warp & 3;           // TMEM lane quarter
-    const int ch = warp >> 2;               // column half of S (and of O)
-    const int r = quarter * 32 + lane;      // query row within the tile
+    const int t = warp >> 2;             // query tile
+    const int quarter = warp & 3;        // TMEM lane quarter
+    const int r = quarter * 32 + lane;   // row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int q_row = q0 + r;
+    const uint32_t s_tm = tmem + lane_off + t * 128;
+    const uint32_t o_tm = tmem + lane_off + 256 + t * 128;
+    const int q_row = q0 + t * kTileM + r;
     const long long vis_row = a.causal ? min((long long)kv_len, (long long)q_off + q_row + 1) : (long long)kv_len;
-    // every row of the tile sees keys [0, vis_min): tiles below it need no mask
-    const long long vis_min = a.causal ? min((long long)kv_len, (long long)q_off + q0 + 1) : (long long)kv_len;
-    float* red = reinterpret_cast<float*>(smem + kRedOff);  // [parity][half][row]
-    const int pair_bar = 1 + quarter;
-    float m_ref = -INFINITY, l_part = 0.f;
+    const long long vis_min =
+        a.causal ? min((long long)kv_len, (long long)q_off + q0 + t * kTileM + 1) : (long long)kv_len;
+    float m_ref = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int sb = j & 1;
-      // every lane returns from the bounded wait; the vote keeps the warp's
-      // decision uniform before any warp-collective tcgen05 instruction
-      if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[sb], (j >> 1) & 1, abort))) {
+      if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[t], j & 1, abort))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[64];
-      tmem_ld32(tmem + lane_off + sb * 128 + ch * 64, sv);
-      tmem_ld32(tmem + lane_off + sb * 128 + ch * 64 + 32, sv + 32);
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 128; c += 32) tmem_ld32(s_tm + c, sv + c);
       tmem_wait_ld();
       if ((long long)(j + 1) * kTileN > vis_min) {
-        const long long vis = vis_row - (long long)j * kTileN - ch * 64;  // visible columns of this half
+        const long long vis = vis_row - (long long)j * kTileN;
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
+        for (int c = 0; c < 128; ++c)
           if (c >= vis) sv[c] = -INFINITY;
       }
-      float mx = sv[0];
+      // eight independent max / sum chains instead of one 128-long chain
+      // three-input max.f32 (sm_100): two new scores per instruction
+      float mx8[8];
 #pragma unroll
-      for (int c = 1; c < 64; ++c) mx = fmaxf(mx, sv[c]);
-      float* rbuf = red + (j & 1) * 2 * kTileM;
-      rbuf[ch * kTileM + r] = mx;
-      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
-      mx = fmaxf(rbuf[r], rbuf[kTileM + r]);
-      const float m_tile = mx * a.scale_log2;  // scale > 0 keeps the order
+      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+      for (int c = 8; c < 128; c += 2)
+        asm("max.f32 %0, %0, %1, %2;" : "+f"(mx8[(c >> 1) & 7]) : "f"(sv[c]), "f"(sv[c + 1]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_tile = mx * a.scale_log2;
       const bool move = m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY);
       const float m_new = move ? m_tile : m_ref;
       const float corr = move ? exp2f(m_ref - m_new) : 1.f;
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      float sum = 0.f;
-      uint32_t pw[32];
-      uint32_t lw[kSplitP ? 32 : 1];
+      // packed fp32 pairs: scale-and-shift, sum and the split residual each take
+      // one FFMA2 / FADD2 per two scores; exp2 is the MUFU instruction
+      // (ex2.approx, relative error ~2^-22, far below the 2^-16 of split P)
+      float2 sum4[4];
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float p0 = exp2f(fmaf(sv[c], a.scale_log2, -m_use));
-        const float p1 = exp2f(fmaf(sv[c + 1], a.scale_log2, -m_use));
-        sum += p0 + p1;
-        const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-        pw[c / 2] = *reinterpret_cast<const uint32_t*>(&pb);
-        if constexpr (kSplitP) {
-          // p - bf16(p) is exact in fp32; its bf16 rounding carries the next 8 bits
-          const float2 hi = __bfloat1622float2(pb);
-          const __nv_bfloat162 lb = __floats2bfloat162_rn(p0 - hi.x, p1 - hi.y);
-          lw[c / 2] = *reinterpret_cast<const uint32_t*>(&lb);
+      for (int i = 0; i < 4; ++i) sum4[i] = make_float2(0.f, 0.f);
+      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
+      const float2 nm2 = make_float2(-m_use, -m_use);
+#pragma unroll
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t pw[16];
+        uint32_t lw[kSplitP ? 16 : 1];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float2 x = __ffma2_rn(make_float2(sv[c + i], sv[c + i + 1]), sc2, nm2);
+          float2 pp;
+          asm("ex2.approx.f32 %0, %1;" : "=f"(pp.x) : "f"(x.x));
+          asm("ex2.approx.f32 %0, %1;" : "=f"(pp.y) : "f"(x.y));
+          sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], pp);
+          const __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
+          const uint32_t hw = *reinterpret_cast<const uint32_t*>(&pb);
+          pw[i / 2] = hw;
+          if constexpr (kSplitP) {
+            // pp - bf16(pp) is exact in fp32; its bf16 rounding carries the next 8 bits
+            const float2 hi = make_float2(__uint_as_float(hw << 16), __uint_as_float(hw & 0xFFFF0000u));
+            const float2 d = __fadd2_rn(pp, make_float2(-hi.x, -hi.y));
+            const __nv_bfloat162 lb = __floats2bfloat162_rn(d.x, d.y);
+            lw[i / 2] = *reinterpret_cast<const uint32_t*>(&lb);
+          }
         }
+        // P_j as bf16 pairs along keys: high part in columns [0, 64), low part in [64, 128)
+        tmem_st16(s_tm + c / 2, pw);
+        if constexpr (kSplitP) tmem_st16(s_tm + 64 + c / 2, lw);
       }
-      l_part = l_part * corr + sum;
-      // P_j (bf16 pairs along keys): high part in columns [0,64), low part in [64,128)
-      tmem_st32(tmem + lane_off + sb * 128 + ch * 32, pw);
-      if constexpr (kSplitP) tmem_st32(tmem + lane_off + sb * 128 + 64 + ch * 32, lw);
+      const float sum = ((sum4[0].x + sum4[0].y) + (sum4[1].x + sum4[1].y)) +
+                        ((sum4[2].x + sum4[2].y) + (sum4[3].x + sum4[3].y));
+      l_run = l_run * corr + sum;
       tmem_wait_st();
-      if (j >= 1) {
-        // O holds sum_{i<j} P_i V_i at the old reference max once PV_{j-1} is done
-        if (!__all_sync(0xffffffffu, wait_or_abort(&bars->o_full, (j - 1) & 1, abort))) {
+      if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+        // O_t must hold PV_t(j-1) before it is rescaled
+        if (!__all_sync(0xffffffffu, wait_or_abort(&bars->o_full[t], (j - 1) & 1, abort))) {
           ok = false;
           break;
         }
-        if (__any_sync(0xffffffffu, corr != 1.f)) {
-          tc_fence_after();
+        tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 64; c += 32) {
-            float ov[32];
-            tmem_ld32(tm_o + lane_off + ch * 64 + c, ov);
-            tmem_wait_ld();
-            uint32_t ow[32];
+        for (int c = 0; c < 128; c += 32) {
+          float ov[32];
+          tmem_ld32(o_tm + c, ov);
+          tmem_wait_ld();
+          uint32_t ow[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ow[i] = __float_as_uint(ov[i] * corr);
-            tmem_st32(tm_o + lane_off + ch * 64 + c, ow);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) ow[i] = __float_as_uint(ov[i] * corr);
+          tmem_st32(o_tm + c, ow);
         }
+        tmem_wait_st();
       }
       m_ref = m_new;
       tc_fence_before();
-      mbar_arrive(&bars->p_full);
+      mbar_arrive(&bars->p_full[t]);
     }
-    // epilogue: O / l -> bf16 (l = sum of the two halves' partial sums)
-    if (ok && __all_sync(0xffffffffu, wait_or_abort(&bars->o_full, (ntiles - 1) & 1, abort))) {
+    // epilogue: O_t / l -> bf16
+    if (ok && __all_sync(0xffffffffu, wait_or_abort(&bars->o_full[t], (ntiles - 1) & 1, abort))) {
       tc_fence_after();
-      float* lbuf = red + (ntiles & 1) * 2 * kTileM;
-      lbuf[ch * kTileM + r] = l_part;
-      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
-      const float l_tot = lbuf[r] + lbuf[kTileM + r];
-      const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
-      uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh + ch * 64;
+      const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
+      uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh;
 #pragma unroll
-      for (int c = 0; c < 64; c += 32) {
+      for (int c = 0; c < 128; c += 32) {
         float ov[32];
-        tmem_ld32(tm_o + lane_off + ch * 64 + c, ov);
+        tmem_ld32(o_tm + c, ov);
         tmem_wait_ld();
         if (q_row < a.n_q) {
 #pragma unroll
@@ -362,16 +381,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (*abort) {
     if (threadIdx.x == 0) atomicOr(a.status, kDevWaitTimeout);
-    // copies issued by the TMA warp must land before the CTA retires
-    if (threadIdx.x == kTmaWarp * 32) {
+    if (threadIdx.x == kPPTmaWarp * 32) {
       (void)mbar_wait_bounded(&bars->q_full, 0);
       const int issued = bars->issued;
-      for (int t = (issued > kStages ? issued - kStages : 0); t < issued; ++t)
-        (void)mbar_wait_bounded(&bars->kv_full[t % kStages], (t / kStages) & 1);
+      for (int j = (issued > kPPStages ? issued - kPPStages : 0); j < issued; ++j)
+        (void)mbar_wait_bounded(&bars->kv_full[j % kPPStages], (j / kPPStages) & 1);
     }
   }
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kPPMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
@@ -449,17 +467,17 @@ cudaError_t prefill_tc_launch(const PrefillTcParams& p, cudaStream_t stream) {
   a.kv_rows = p.kv_rows;
   a.scale_log2 = p.scale_log2;
   a.status = p.status;
-  dim3 grid(p.n_q_heads, (p.n_q + kTileM - 1) / kTileM, p.batch);
+  dim3 grid2(p.n_q_heads, (p.n_q + 2 * kTileM - 1) / (2 * kTileM), p.batch);
   if (p.split_p) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemAlloc);
+    cudaError_t e = cudaFuncSetAttribute(prefill_pp_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kPPSmemAlloc);
     if (e != cudaSuccess) return e;
-    prefill_tc_kernel<true><<<grid, kThreads, kSmemAlloc, stream>>>(mq, mk, mv, a);
+    prefill_pp_kernel<true><<<grid2, kPPThreads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
   } else {
-    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemAlloc);
+    cudaError_t e = cudaFuncSetAttribute(prefill_pp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kPPSmemAlloc);
     if (e != cudaSuccess) return e;
-    prefill_tc_kernel<false><<<grid, kThreads, kSmemAlloc, stream>>>(mq, mk, mv, a);
+    prefill_pp_kernel<false><<<grid2, kPPThreads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
   }
   return cudaGetLastError();
 }
