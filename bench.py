@@ -71,6 +71,8 @@ def parse_args():
     ap.add_argument("--paged", type=int, default=0, metavar="PAGE_SIZE",
                     help="configs 2/3: decode from a paged cache (page pool in shuffled page order, block "
                          "table) instead of the contiguous cache; 0 = contiguous")
+    ap.add_argument("--paged-order", choices=["random", "sequential"], default="random",
+                    help="page assignment of the paged cache (random permutation or consecutive pages)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
@@ -334,7 +336,8 @@ def _setup_decode(args, cfg, rank, world, dev):
         pps = math.ceil(L / ps)
         npg = [math.ceil(int(n) / ps) for n in lens_np]
         total = sum(npg)
-        perm = torch.randperm(total, generator=torch.Generator().manual_seed(7)).to(dev)
+        perm = (torch.randperm(total, generator=torch.Generator().manual_seed(7)) if args.paged_order == "random"
+                else torch.arange(total)).to(dev)
         table = torch.full((B, pps), -1, dtype=torch.int32, device=dev)
         kp = torch.empty((total, cfg.n_kv_heads, ps, cfg.head_dim), dtype=k.dtype, device=dev)
         vp = torch.empty_like(kp)
@@ -362,7 +365,7 @@ def _setup_decode(args, cfg, rank, world, dev):
                 plan.chunk_tokens, dec.workspace.data_ptr(), dec.workspace.numel(), stream.cuda_stream),
                 "decode_paged")
         launches = 1
-        info["paged"] = {"page_size": ps, "pages": total, "page_order": "random permutation (seed 7)",
+        info["paged"] = {"page_size": ps, "pages": total, "page_order": ("random permutation (seed 7)" if args.paged_order == "random" else "sequential"),
                          "layout": "[pages][Hkv][page_size][D]"}
     else:
         dec = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, L, dev, lens=lens_np,
