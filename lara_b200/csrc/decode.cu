@@ -146,17 +146,22 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   constexpr int V = T::kVec;
   extern __shared__ __align__(128) uint8_t smem[];
 
-  const int split = blockIdx.x;
-  const int kvh = blockIdx.y;
-  const int b = blockIdx.z;                  // query row
+  // grid (kv head, row, split): every CTA of split 0 launches before any of
+  // split 1, so a larger first chunk fills the SMs and the shorter ones fill
+  // the tail
+  const int split = blockIdx.z;
+  const int kvh = blockIdx.x;
+  const int b = blockIdx.y;                  // query row
   const int seq = b / p.rows_per_seq;        // its K/V stream
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const bool partial_out = p.out_acc != nullptr;
 
   const int len = seq_len_of(p, seq, b - seq * p.rows_per_seq);
-  const int tok_begin = split * p.chunk;
-  const int nsplit_b = (len + p.chunk - 1) / p.chunk;
+  // split 0 covers [0, c0), split s >= 1 covers [c0 + (s-1)*chunk, c0 + s*chunk)
+  const int c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
+  const int tok_begin = split == 0 ? 0 : c0 + (split - 1) * p.chunk;
+  const int nsplit_b = len <= c0 ? 1 : 1 + (len - c0 + p.chunk - 1) / p.chunk;
 
   if (len == 0) {
     // No key is visible: the output is zero (the RTL normaliser maps l == 0
@@ -177,7 +182,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     return;
   }
   if (tok_begin >= len) return;
-  const int ntok = min(len - tok_begin, p.chunk);
+  const int ntok = min(len - tok_begin, split == 0 ? c0 : p.chunk);
   const int ntiles = (ntok + T::kTile - 1) / T::kTile;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::kBarOff);
@@ -601,18 +606,30 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
   *chunk_out = best_chunk;
 }
 
+int decode_first_chunk(int nsplit, int chunk, int group, int head_dim) {
+  if (nsplit != 2) return 0;
+  const int tile = decode_tile_tokens(head_dim, group);
+  if (tile <= 0) return 0;
+  const long long span = 2ll * chunk;
+  const int c0 = (int)((span * 7 / 8) / tile * tile);
+  return c0 > chunk ? c0 : 0;  // c0 + chunk >= 2 * chunk covers what the plan covered
+}
+
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream) {
   const int group = p.n_q_heads / p.n_kv_heads;
   const KernelInfo k = lookup(p.head_dim, group);
   if (!k.fn) return cudaErrorInvalidValue;
   if (p.chunk <= 0 || p.chunk % k.tile != 0 || p.nsplit <= 0) return cudaErrorInvalidValue;
+  if (p.chunk0 < 0 || p.chunk0 % k.tile != 0) return cudaErrorInvalidValue;
   // The splits must cover every token a sequence may hold, or the last-CTA
   // merge of a longer sequence would never see all of its splits.
-  if ((long long)p.nsplit * p.chunk < (long long)p.max_seq_len) return cudaErrorInvalidValue;
+  const long long c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
+  if (c0 + (long long)(p.nsplit - 1) * p.chunk < (long long)p.max_seq_len) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
   if (e != cudaSuccess) return e;
   if (p.rows_per_seq < 1 || p.batch > 65535) return cudaErrorInvalidValue;
-  dim3 grid(p.nsplit, p.n_kv_heads, p.batch);
+  if (p.nsplit > 65535) return cudaErrorInvalidValue;
+  dim3 grid(p.n_kv_heads, p.batch, p.nsplit);
   void* args[] = {const_cast<DecodeParams*>(&p)};
   return cudaLaunchKernel(k.fn, grid, dim3(k.threads), args, k.smem, stream);
 }
