@@ -374,7 +374,22 @@ class AttentionAccelerator:
                           bitstream_sha256=self._bitstream_hash, clock_mhz=self._pl_clock_mhz, seq_len=seq_len,
                           causal=causal, q_pos_base=q_pos_base, kv_pos_base=kv_pos_base)
 
-    def _finish_profile(self, prof: RunProfile, t_start: float) -> None:
+    @property
+    def last_profile(self) -> RunProfile | None:
+        # run_query finishes its profile only when it is read (the device times
+        # come from CUDA events; reading them is work a decode loop need not pay)
+        pending = self.__dict__.get("_pending_profile")
+        if pending is not None:
+            self._pending_profile = None
+            self._finish_profile(*pending)
+        return self.__dict__.get("_last_profile")
+
+    @last_profile.setter
+    def last_profile(self, prof: RunProfile | None) -> None:
+        self._pending_profile = None
+        self._last_profile = prof
+
+    def _finish_profile(self, prof: RunProfile, t_start: float, t_end: float | None = None) -> None:
         perf = self.read_perf()
         prof.pl_total_cycles = perf["cycles"]
         prof.pl_mac_cycles = perf["mac_cycles"]
@@ -385,7 +400,7 @@ class AttentionAccelerator:
         prof.pl_mac_ms = perf["mac_cycles"] / per_ms
         prof.pl_stall_ms = perf["stall_cycles"] / per_ms
         prof.pl_core_active_ms_excluding_stalls = prof.pl_core_active_cycles_excluding_stalls / per_ms
-        prof.attention_total_ms = (time.perf_counter() - t_start) * 1000.0
+        prof.attention_total_ms = ((time.perf_counter() if t_end is None else t_end) - t_start) * 1000.0
 
     def run_attention(self, q_heads: np.ndarray, k_heads: np.ndarray, v_heads: np.ndarray, *,
                       seq_len: int | None = None, q_pos_base: int = 0, kv_pos_base: int = 0, causal: bool = True,
@@ -582,7 +597,7 @@ class AttentionAccelerator:
         prof.q_dma_transfers, prof.q_dma_bytes = 1, qw.nbytes
         prof.output_dma_transfers, prof.output_dma_bytes = 1, out.nbytes
         self._last_output = out
-        self._finish_profile(prof, t_start)
+        self._pending_profile = (prof, t_start, time.perf_counter())
         return out
 
     def run_prefill_chunk(self, q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, *,

@@ -539,6 +539,7 @@ struct lara_ctx {
   bool plan_valid = false;
   lara_perf perf{};
   bool have_perf = false;
+  bool perf_pending = false;  // events of the last transaction not yet read
 };
 
 namespace {
@@ -599,7 +600,15 @@ int ctx_finish(lara_ctx* c) {
   return LARA_OK;
 }
 
+// The device times of the last transaction are read from its events when
+// lara_read_perf asks (the events stay recorded until the next transaction).
 void ctx_record_perf(lara_ctx* c) {
+  c->perf_pending = true;
+  c->have_perf = true;
+}
+
+void ctx_resolve_perf(lara_ctx* c) {
+  if (!c->perf_pending) return;
   float total = 0.f, mac = 0.f;
   cudaEventElapsedTime(&total, c->ev[0], c->ev[3]);
   cudaEventElapsedTime(&mac, c->ev[1], c->ev[2]);
@@ -608,7 +617,7 @@ void ctx_record_perf(lara_ctx* c) {
   if (c->perf.mac_cycles > c->perf.cycles) c->perf.mac_cycles = c->perf.cycles;
   c->perf.stall_cycles = c->perf.cycles - c->perf.mac_cycles;
   c->perf.clock_mhz = 1000.0;
-  c->have_perf = true;
+  c->perf_pending = false;
 }
 
 int ctx_alloc(lara_ctx* c) {
@@ -1082,6 +1091,8 @@ int lara_read_perf(lara_ctx* c, lara_perf* out) {
   if (rc) return rc;
   if (!out) return fail(LARA_ERR_STREAM_DEST, "null pointer");
   if (c->have_perf) {
+    DeviceGuard g(c->device);
+    ctx_resolve_perf(c);
     *out = c->perf;
   } else {
     *out = lara_perf{0, 0, 0, 1000.0};

@@ -33,6 +33,9 @@
 //    partials and writes the bf16 output.
 #include <cmath>
 #include <cstdio>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "common.cuh"
 #include "lara_internal.h"
@@ -625,8 +628,20 @@ cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream) {
   // merge of a longer sequence would never see all of its splits.
   const long long c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
   if (c0 + (long long)(p.nsplit - 1) * p.chunk < (long long)p.max_seq_len) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
-  if (e != cudaSuccess) return e;
+  {
+    // the shared-memory opt-in is per (kernel, device): set it once
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done.count({k.fn, dev})) {
+      e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+      if (e != cudaSuccess) return e;
+      done.insert({k.fn, dev});
+    }
+  }
   if (p.rows_per_seq < 1 || p.batch > 65535) return cudaErrorInvalidValue;
   if (p.nsplit > 65535) return cudaErrorInvalidValue;
   dim3 grid(p.n_kv_heads, p.batch, p.nsplit);
