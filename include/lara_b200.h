@@ -383,6 +383,17 @@ LARA_API int lara_run_layer(lara_ctx* ctx, const uint16_t* x, const uint16_t* w_
                             int hidden, uint16_t* o, float rms_eps, float rope_base, int on_device);
 LARA_API int lara_read_layer_perf(lara_ctx* ctx, uint64_t* prologue_ns, uint64_t* attention_ns);
 
+/* Failure-detection self tests (no reference counterpart; the RTL reports
+ * timeouts through ERROR_CODE / STATUS_ERROR, sw/attn_driver.py:446-454).
+ * A kernel waits, with the bounded wait every pipeline wait uses, on an
+ * mbarrier phase that nothing completes; after limit_us (1 .. 2e6) it gives up
+ * and sets the timeout bit of the status word -- no fault, no hang.
+ * lara_selftest_wait_timeout writes the word at workspace[0] (read it with
+ * lara_workspace_status); lara_ctx_selftest_timeout runs it on the context's
+ * stream and returns LARA_ERR_TIMEOUT, after which the context is usable. */
+LARA_API int lara_selftest_wait_timeout(void* workspace, int limit_us, void* stream);
+LARA_API int lara_ctx_selftest_timeout(lara_ctx* ctx, int limit_us);
+
 /* Replaces: read_perf (sw/attn_driver.py:466-467, CSRs 0x100/0x108/0x10C). */
 LARA_API int lara_read_perf(lara_ctx* ctx, lara_perf* out);
 

@@ -72,6 +72,7 @@ SIGNATURES = {
     "lara_last_error_string": (c_char_p, []),
     "lara_status_name": (c_char_p, [c_int]),
     "lara_device_count": (c_int, [POINTER(c_int)]),
+    "lara_selftest_wait_timeout": (c_int, [c_void_p, c_int, c_void_p]),
     "lara_device_query": (c_int, [c_int, POINTER(LaraDeviceInfo)]),
     "lara_decode_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, POINTER(c_int), POINTER(c_int)]),
     "lara_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
@@ -122,6 +123,7 @@ SIGNATURES = {
     "lara_read_layer_perf": (c_int, [c_void_p, POINTER(c_uint64), POINTER(c_uint64)]),
     "lara_sync": (c_int, [c_void_p, c_int]),
     "lara_ctx_device": (c_int, [c_void_p]),
+    "lara_ctx_selftest_timeout": (c_int, [c_void_p, c_int]),
     "lara_set_arithmetic": (c_int, [c_void_p, c_int]),
     "lara_get_arithmetic": (c_int, [c_void_p]),
 }

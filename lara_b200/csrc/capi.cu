@@ -1086,6 +1086,15 @@ int lara_read_layer_perf(lara_ctx* c, uint64_t* prologue_ns, uint64_t* attention
   return LARA_OK;
 }
 
+int lara_ctx_selftest_timeout(lara_ctx* c, int limit_us) {
+  int rc = ctx_check(c);
+  if (rc) return rc;
+  if (limit_us < 1 || limit_us > 2000000) return fail(LARA_ERR_BAD_CFG, "limit_us must be in [1, 2e6]");
+  DeviceGuard g(c->device);
+  LARA_CUDA(lara::selftest_wait_launch(static_cast<int*>(c->ws), limit_us, c->stream));
+  return ctx_finish(c);  // LARA_ERR_TIMEOUT, and the status word is cleared for the next call
+}
+
 int lara_read_perf(lara_ctx* c, lara_perf* out) {
   int rc = ctx_check(c);
   if (rc) return rc;

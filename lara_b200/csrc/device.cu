@@ -7,6 +7,7 @@
 #include <cstring>
 
 #include "../../include/lara_b200.h"
+#include "common.cuh"
 #include "lara_internal.h"
 
 namespace {
@@ -17,7 +18,39 @@ __global__ void image_probe_kernel(int* p) {
   if (p) *p = 0;
 }
 
+// Failure-detection self test: every thread waits, with the same bounded wait
+// the attention kernels use, on an mbarrier phase that nothing completes.  The
+// wait gives up after limit_ns and the kernel reports kDevWaitTimeout in the
+// status word -- the path a stuck pipeline takes -- without faulting.
+__global__ void selftest_wait_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    lara::mbar_init(&bar, 1);
+    lara::mbar_fence_init();
+  }
+  __syncthreads();
+  const bool ok = lara::mbar_wait_bounded(&bar, 0, limit_ns);
+  if (!__syncthreads_and(ok) && threadIdx.x == 0) atomicOr(status, lara::kDevWaitTimeout);
+}
+
 }  // namespace
+
+namespace lara {
+cudaError_t selftest_wait_launch(int* status, int limit_us, cudaStream_t stream) {
+  selftest_wait_kernel<<<1, 64, 0, stream>>>(status, (unsigned long long)limit_us * 1000ull);
+  return cudaGetLastError();
+}
+}  // namespace lara
+
+extern "C" int lara_selftest_wait_timeout(void* workspace, int limit_us, void* stream) {
+  if (!workspace) return lara::set_last_error(LARA_ERR_STREAM_DEST, "null workspace");
+  if (limit_us < 1 || limit_us > 2000000) return lara::set_last_error(LARA_ERR_BAD_CFG, "limit_us must be in [1, 2e6]");
+  const cudaError_t e = lara::selftest_wait_launch(static_cast<int*>(workspace), limit_us,
+                                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return lara::set_last_error(LARA_ERR_CUDA, std::string("self-test launch: ") + cudaGetErrorString(e));
+  return LARA_OK;
+}
 
 extern "C" int lara_device_count(int* count) {
   if (!count) return lara::set_last_error(LARA_ERR_STREAM_DEST, "null output pointer");

@@ -91,6 +91,10 @@ int decode_first_chunk(int nsplit, int chunk, int group, int head_dim);
 
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream);
 
+// Failure-detection self test: a bounded wait on a phase nothing completes;
+// sets kDevWaitTimeout in *status after limit_us.
+cudaError_t selftest_wait_launch(int* status, int limit_us, cudaStream_t stream);
+
 // Tensor-core (tcgen05/TMEM) attention of n_q query rows per sequence over a
 // bf16 KV cache [batch][Hkv][kv_rows][128].  Sequence b has
 // kv_len = base + kv_add keys (base = base_lens[b] or 0) and query row i sees
