@@ -68,6 +68,8 @@ struct Traits {
   static constexpr int kH = cmin(kLogLPT, ilog2(kNV));       // reduce-scatter steps
   static constexpr int kR = kLogLPT - kH;                    // duplicate-lane butterfly steps
   static constexpr int kLogG = ilog2(G);
+  static constexpr int kLogIter = ilog2(kIter);
+  static constexpr int kHP = cmin(kH, kLogIter);             // steps split on a pass bit (no select)
   static constexpr int kMinBlocks = 2;
   // shared memory layout
   static constexpr int kRingBytes = kStages * kStageBytes;
@@ -224,6 +226,13 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
 
   const int half = lane / T::kLPT;            // which token row of the pass
   const int c = lane % T::kLPT;               // vector slot of the row
+  // Pass order of this lane: reduce-scatter step s (< kHP) splits on pass bit
+  // kLogIter - 1 - s with partner offset kLPT >> (s + 1); a lane whose offset
+  // bit is set takes that pass bit flipped, so its kept half sits in the low slots.
+  int xperm = 0;
+#pragma unroll
+  for (int s2 = 0; s2 < T::kHP; ++s2)
+    xperm |= ((c >> (T::kLogLPT - 1 - s2)) & 1) << (T::kLogIter - 1 - s2);
   const int t_slot = c >> T::kR;              // finished-score slot after reduce-scatter
   const int my_g = t_slot % G;                // head of that score
   const int my_it = t_slot / G;               // pass of that score
@@ -256,11 +265,12 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     const int nvalid = min(T::kTile, ntok - i * T::kTile) - warp * T::kTokPerWarp;
 
     // QK^T: ITER token rows x G heads of partial dot products over V dims,
-    // accumulated as (even, odd) dim pairs with packed fp32 FMA.
+    // accumulated as (even, odd) dim pairs with packed fp32 FMA.  Slot
+    // it * G + g holds pass it ^ xperm of head g (see the reduce-scatter).
     float part[T::kNV];
 #pragma unroll
     for (int it = 0; it < T::kIter; ++it) {
-      const int tw = it * T::kTPI + half;
+      const int tw = (it ^ xperm) * T::kTPI + half;
       float2 kp[V2];
       load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Kt + tw * T::kRowBytes) + c * V, kp);
 #pragma unroll
@@ -272,17 +282,25 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
       }
     }
     // Reduce-scatter over the row's lanes: each step halves the values a lane
-    // keeps and adds the partner's matching half.
+    // keeps and adds the partner's matching half.  In the first kHP steps the
+    // half boundary is a bit of the pass index; there every lane already
+    // holds the half it keeps in the low slots (its passes were taken in the
+    // order it ^ xperm), so it sends the high slots without selecting.
 #pragma unroll
     for (int step = 0; step < T::kH; ++step) {
       const int off = T::kLPT >> (step + 1);
       const int nv = T::kNV >> step;
-      const bool upper = (lane & off) != 0;
+      if (step < T::kHP) {
 #pragma unroll
-      for (int j = 0; j < nv / 2; ++j) {
-        const float send = upper ? part[j] : part[j + nv / 2];
-        const float keep = upper ? part[j + nv / 2] : part[j];
-        part[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        for (int j = 0; j < nv / 2; ++j) part[j] += __shfl_xor_sync(0xffffffffu, part[j + nv / 2], off);
+      } else {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int j = 0; j < nv / 2; ++j) {
+          const float send = upper ? part[j] : part[j + nv / 2];
+          const float keep = upper ? part[j + nv / 2] : part[j];
+          part[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
       }
     }
 #pragma unroll
