@@ -69,7 +69,7 @@ struct Traits {
   static constexpr int kR = kLogLPT - kH;                    // duplicate-lane butterfly steps
   static constexpr int kLogG = ilog2(G);
   static constexpr int kLogIter = ilog2(kIter);
-  static constexpr int kHP = cmin(kH, kLogIter);             // steps split on a pass bit (no select)
+  static constexpr int kHP = cmin(kH, kLogIter);             // steps split on a pass bit (the rest on a head bit)
   static constexpr int kMinBlocks = 2;
   // shared memory layout
   static constexpr int kRingBytes = kStages * kStageBytes;
@@ -233,6 +233,12 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
 #pragma unroll
   for (int s2 = 0; s2 < T::kHP; ++s2)
     xperm |= ((c >> (T::kLogLPT - 1 - s2)) & 1) << (T::kLogIter - 1 - s2);
+  // Likewise the later steps split on a head bit: this lane keeps the query of
+  // head g ^ yperm in register slot g, so those steps need no select either.
+  int yperm = 0;
+#pragma unroll
+  for (int s2 = T::kHP; s2 < T::kH; ++s2)
+    yperm |= ((c >> (T::kLogLPT - 1 - s2)) & 1) << (T::kLogG - 1 - (s2 - T::kLogIter));
   const int t_slot = c >> T::kR;              // finished-score slot after reduce-scatter
   const int my_g = t_slot % G;                // head of that score
   const int my_it = t_slot / G;               // pass of that score
@@ -244,7 +250,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   float2 qp[G][V2];
 #pragma unroll
   for (int g = 0; g < G; ++g)
-    load_bf16_pairs<V>(p.q + b * p.q_sb + (long long)(kvh * G + g) * p.q_sh + c * V, qp[g]);
+    load_bf16_pairs<V>(p.q + b * p.q_sb + (long long)(kvh * G + (g ^ yperm)) * p.q_sh + c * V, qp[g]);
   float2 acc[G][V2];
 #pragma unroll
   for (int g = 0; g < G; ++g)
@@ -282,26 +288,17 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
       }
     }
     // Reduce-scatter over the row's lanes: each step halves the values a lane
-    // keeps and adds the partner's matching half.  In the first kHP steps the
-    // half boundary is a bit of the pass index; there every lane already
-    // holds the half it keeps in the low slots (its passes were taken in the
-    // order it ^ xperm), so it sends the high slots without selecting.
+    // keeps and adds the partner's matching half.  Each step's half boundary
+    // is a bit of the pass index (first kHP steps) or of the head index; every
+    // lane took its passes in the order it ^ xperm and holds head g ^ yperm in
+    // slot g, so the half it keeps is always in its low slots and it simply
+    // sends the high slots.
 #pragma unroll
     for (int step = 0; step < T::kH; ++step) {
       const int off = T::kLPT >> (step + 1);
       const int nv = T::kNV >> step;
-      if (step < T::kHP) {
 #pragma unroll
-        for (int j = 0; j < nv / 2; ++j) part[j] += __shfl_xor_sync(0xffffffffu, part[j + nv / 2], off);
-      } else {
-        const bool upper = (lane & off) != 0;
-#pragma unroll
-        for (int j = 0; j < nv / 2; ++j) {
-          const float send = upper ? part[j] : part[j + nv / 2];
-          const float keep = upper ? part[j + nv / 2] : part[j];
-          part[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-      }
+      for (int j = 0; j < nv / 2; ++j) part[j] += __shfl_xor_sync(0xffffffffu, part[j + nv / 2], off);
     }
 #pragma unroll
     for (int step = 0; step < T::kR; ++step) {
