@@ -275,3 +275,41 @@ def test_config3_ragged_sampled(dev):
         gold = oracle.decode_attention(qw[b:b + 1], kw, vw, np.array([n]))
         g64 = oracle.decode_attention_fp64(qw[b:b + 1], kw, vw, np.array([n]))
         assert_bf16_parity(o[b:b + 1], gold, g64, what=f"cfg3 b={b} len={n}")
+
+
+@pytest.mark.slow
+def test_config4_long_context_sampled(dev):
+    """Config 4's sequence length (1,048,576 cached tokens, N(0,1)*0.5, seed 3) for
+    two sequences: the single-GPU decode (the planner's many-split plan) and the
+    split-KV path -- four token ranges decoded as partials and merged by the LSE
+    combine, as four GPUs would -- both within the tolerance of the oracle on
+    sampled kv heads."""
+    import torch
+
+    from lara_b200 import ops, parallel
+    from lara_b200.workloads import CONFIGS, make_decode_inputs
+
+    cfg = CONFIGS[4]
+    B, L = 2, cfg.seq_len
+    q, k, v, lens = make_decode_inputs(cfg, dev, batch=B)
+    dec = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, L, dev)
+    o_full = words_of(dec(q, k, v, lens))
+    mls, accs = [], []
+    for r in range(4):
+        start, cnt = parallel.token_range(L, 4, r)
+        kr, vr = k[:, :, start:start + cnt].contiguous(), v[:, :, start:start + cnt].contiguous()
+        part = ops.Decoder(B, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, cnt, dev)
+        ml, acc = part.partial(q, kr, vr, torch.full((B,), cnt, dtype=torch.int32, device=dev))
+        mls.append(ml)
+        accs.append(acc)
+        del kr, vr
+    o_split = words_of(ops.lse_combine(torch.stack(mls), torch.stack(accs)).view(B, cfg.n_q_heads, cfg.head_dim))
+    qw = words_of(q)
+    G = cfg.group
+    for b, h in ((0, 0), (1, 5)):
+        kw, vw = words_of(k[b:b + 1, h:h + 1]), words_of(v[b:b + 1, h:h + 1])
+        qs = qw[b:b + 1, h * G:(h + 1) * G]
+        gold = oracle.decode_attention(qs, kw, vw, np.array([L]))
+        g64 = oracle.decode_attention_fp64(qs, kw, vw, np.array([L]))
+        assert_bf16_parity(o_full[b, h * G:(h + 1) * G], gold[0], g64[0], what=f"cfg4 full b={b} kvh={h}")
+        assert_bf16_parity(o_split[b, h * G:(h + 1) * G], gold[0], g64[0], what=f"cfg4 split b={b} kvh={h}")
