@@ -53,7 +53,7 @@ int check_geometry(int batch, int hq, int hkv, int d, int lmax) {
   if (hq % hkv != 0) return fail(LARA_ERR_BAD_CFG, "n_q_heads (%d) must be a multiple of n_kv_heads (%d)", hq, hkv);
   if (lara::decode_tile_tokens(d, hq / hkv) == 0)
     return fail(LARA_ERR_UNSUPPORTED, "no kernel compiled for head_dim=%d group=%d (supported: head_dim 64/128, "
-                "group 1,2,4,8 (and 16 for head_dim 128))", d, hq / hkv);
+                "group 1, 2, 4, 8)", d, hq / hkv);
   if (batch > 65535) return fail(LARA_ERR_BAD_CFG, "batch %d exceeds 65535", batch);
   return LARA_OK;
 }
@@ -185,6 +185,8 @@ int dense_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16
   if (!q || !k || !v || !o || !ws) return fail(LARA_ERR_STREAM_DEST, "null tensor or workspace pointer");
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 4) || !aligned(ws, 256))
     return fail(LARA_ERR_STREAM_DEST, "q/k/v must be 16-byte aligned, o 4-byte, workspace 256-byte");
+  if (!(scale > 0.f) || !std::isfinite(scale)) return fail(LARA_ERR_BAD_CFG, "scale must be positive and finite");
+  if (ws_bytes < 256) return fail(LARA_ERR_RESULT_LEN, "workspace has %zu bytes, at least 256 needed", ws_bytes);
   {
     lara::PrefillTcParams tp{};
     tp.q = q; tp.q_sb = (long long)hq * L * d; tp.q_sr = d; tp.q_sh = (long long)L * d;
@@ -248,6 +250,7 @@ int prefill_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(o, 4) || !aligned(ws, 256))
     return fail(LARA_ERR_STREAM_DEST, "q/k/v must be 16-byte aligned, o 4-byte, workspace 256-byte");
   if (!(scale > 0.f) || !std::isfinite(scale)) return fail(LARA_ERR_BAD_CFG, "scale must be positive and finite");
+  if (ws_bytes < 256) return fail(LARA_ERR_RESULT_LEN, "workspace has %zu bytes, at least 256 needed", ws_bytes);
   {
     lara::PrefillTcParams tp{};
     tp.q = q; tp.q_sb = (long long)n_new * hq * d; tp.q_sr = (long long)hq * d; tp.q_sh = d;
