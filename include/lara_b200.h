@@ -394,6 +394,18 @@ LARA_API int lara_read_layer_perf(lara_ctx* ctx, uint64_t* prologue_ns, uint64_t
 LARA_API int lara_selftest_wait_timeout(void* workspace, int limit_us, void* stream);
 LARA_API int lara_ctx_selftest_timeout(lara_ctx* ctx, int limit_us);
 
+/* Asynchronous, stream-ordered forms on device buffers (the reference's
+ * start() / wait_done() split, sw/attn_driver.py:361-464): they return once
+ * the work is queued on `stream` (NULL: the context's stream); lara_sync then
+ * waits for it and reports the device status word.  All calls on one context
+ * must be ordered (one stream, or synchronised); they are ordered after the
+ * context's earlier work automatically.
+ * lara_decode: q[B][Hq][D] -> o[B][Hq][D] over the resident cache; splits = 0
+ * uses the planner.  lara_prefill: lara_run_prefill_chunk on device buffers. */
+LARA_API int lara_decode(lara_ctx* ctx, const uint16_t* q, uint16_t* o, int splits, void* stream);
+LARA_API int lara_prefill(lara_ctx* ctx, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new, uint16_t* o,
+                          int n_new, int causal, void* stream);
+
 /* Replaces: read_perf (sw/attn_driver.py:466-467, CSRs 0x100/0x108/0x10C). */
 LARA_API int lara_read_perf(lara_ctx* ctx, lara_perf* out);
 

@@ -122,6 +122,8 @@ SIGNATURES = {
     "lara_run_layer": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_float, c_float, c_int]),
     "lara_read_layer_perf": (c_int, [c_void_p, POINTER(c_uint64), POINTER(c_uint64)]),
     "lara_sync": (c_int, [c_void_p, c_int]),
+    "lara_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "lara_prefill": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "lara_ctx_device": (c_int, [c_void_p]),
     "lara_ctx_selftest_timeout": (c_int, [c_void_p, c_int]),
     "lara_set_arithmetic": (c_int, [c_void_p, c_int]),

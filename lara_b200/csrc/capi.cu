@@ -543,6 +543,7 @@ struct lara_ctx {
   lara_perf perf{};
   bool have_perf = false;
   bool perf_pending = false;  // events of the last transaction not yet read
+  bool async_pending = false; // lara_decode / lara_prefill issued, lara_sync not yet called
 };
 
 namespace {
@@ -1118,14 +1119,104 @@ int lara_sync(lara_ctx* c, int timeout_ms) {
   DeviceGuard g(c->device);
   const auto t0 = std::chrono::steady_clock::now();
   while (true) {
-    cudaError_t e = cudaStreamQuery(c->stream);
-    if (e == cudaSuccess) return LARA_OK;
+    // the last asynchronous call (lara_decode / lara_prefill) ends with ev[3]
+    // on its stream; synchronous calls leave both already complete
+    cudaError_t e = c->async_pending ? cudaEventQuery(c->ev[3]) : cudaStreamQuery(c->stream);
+    if (e == cudaSuccess) break;
     if (e != cudaErrorNotReady) return cuda_fail(e, "stream query");
     if (timeout_ms >= 0 &&
         std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
       return fail(LARA_ERR_TIMEOUT, "attention accelerator timed out after %d ms", timeout_ms);
     std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
+  c->async_pending = false;
+  return ctx_finish(c);  // device status word of the work just completed
+}
+
+int lara_decode(lara_ctx* c, const uint16_t* q, uint16_t* o, int splits, void* stream) {
+  int rc = ctx_check(c);
+  if (rc) return rc;
+  if (!q || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
+  DeviceGuard g(c->device);
+  const cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  int ns = 0, ch = 0;
+  if (splits > 0) {
+    const int tile = lara::decode_tile_tokens(c->d, c->hq / c->hkv);
+    ch = ((c->lmax + splits - 1) / splits + tile - 1) / tile * tile;
+    ns = (c->lmax + ch - 1) / ch;
+  } else {
+    if (!c->plan_valid) {
+      c->plan_split = 0;
+      c->plan_chunk = 0;
+      lara::decode_plan(c->batch, c->hkv, c->hq, c->d, c->lmax, c->lens_host.data(), &c->plan_split,
+                        &c->plan_chunk);
+      c->plan_valid = true;
+    }
+    ns = c->plan_split;
+    ch = c->plan_chunk;
+  }
+  rc = ctx_ensure_ws(c, lara::decode_workspace_layout(c->batch, c->hq, c->hkv, c->d, ns).total);
+  if (rc) return rc;
+  // the context's buffers are ordered on its stream; make the caller's stream wait for them
+  if (st != c->stream) {
+    LARA_CUDA(cudaEventRecord(c->ev[0], c->stream));
+    LARA_CUDA(cudaStreamWaitEvent(st, c->ev[0], 0));
+  }
+  LARA_CUDA(cudaEventRecord(c->ev[0], st));
+  LARA_CUDA(cudaEventRecord(c->ev[1], st));
+  rc = decode_common(q, c->k_cache, c->v_cache, c->lens_dev, o, nullptr, nullptr, c->batch, c->hq, c->hkv, c->d,
+                     c->lmax, 1.0f / std::sqrt((float)c->d), ns, ch, c->ws, c->ws_bytes, st);
+  if (rc) return rc;
+  LARA_CUDA(cudaEventRecord(c->ev[2], st));
+  LARA_CUDA(cudaEventRecord(c->ev[3], st));
+  if (st != c->stream) LARA_CUDA(cudaStreamWaitEvent(c->stream, c->ev[3], 0));
+  c->async_pending = true;
+  ctx_record_perf(c);
+  return LARA_OK;
+}
+
+int lara_prefill(lara_ctx* c, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new, uint16_t* o,
+                 int n_new, int causal, void* stream) {
+  int rc = ctx_check(c);
+  if (rc) return rc;
+  if (!q || !k_new || !v_new || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
+  if (!aligned(q, 16) || !aligned(k_new, 16) || !aligned(v_new, 16) || !aligned(o, 4))
+    return fail(LARA_ERR_STREAM_DEST, "q/k/v must be 16-byte aligned device buffers, o 4-byte");
+  if (n_new < 1) return fail(LARA_ERR_STREAM_LEN, "n_new must be >= 1");
+  for (int b = 0; b < c->batch; ++b)
+    if (c->lens_host[b] + n_new > c->lmax)
+      return fail(LARA_ERR_STREAM_LEN, "prefill of %d tokens overflows sequence %d (len %d, capacity %d)", n_new, b,
+                  c->lens_host[b], c->lmax);
+  DeviceGuard g(c->device);
+  const cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  int ns = 0, ch = 0;
+  const size_t need = prefill_ws_bytes(c->batch, n_new, c->hq, c->hkv, c->d, c->lmax, &ns, &ch);
+  if (need == 0 || (long long)c->batch * n_new > 65535)
+    return fail(LARA_ERR_BAD_CFG, "batch*n_new (%lld) exceeds 65535 query rows", (long long)c->batch * n_new);
+  rc = ctx_ensure_ws(c, need);
+  if (rc) return rc;
+  if (st != c->stream) {
+    LARA_CUDA(cudaEventRecord(c->ev[0], c->stream));
+    LARA_CUDA(cudaStreamWaitEvent(st, c->ev[0], 0));
+  }
+  LARA_CUDA(cudaEventRecord(c->ev[0], st));
+  LARA_CUDA(cudaMemcpyAsync(c->lens_prev_dev, c->lens_dev, sizeof(int32_t) * c->batch, cudaMemcpyDeviceToDevice,
+                            st));
+  LARA_CUDA(cudaEventRecord(c->ev[1], st));
+  cudaError_t e = lara::kv_append_launch(c->k_cache, c->v_cache, c->lens_dev, k_new, v_new, c->batch, c->hkv, c->d,
+                                         c->lmax, n_new, static_cast<int*>(c->ws), st);
+  if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+  rc = prefill_common(q, c->k_cache, c->v_cache, c->lens_prev_dev, o, c->batch, n_new, c->hq, c->hkv, c->d, c->lmax,
+                      causal, 1.0f / std::sqrt((float)c->d), c->ws, c->ws_bytes, st);
+  if (rc) return rc;
+  LARA_CUDA(cudaEventRecord(c->ev[2], st));
+  LARA_CUDA(cudaEventRecord(c->ev[3], st));
+  if (st != c->stream) LARA_CUDA(cudaStreamWaitEvent(c->stream, c->ev[3], 0));
+  for (auto& l : c->lens_host) l += n_new;
+  c->plan_valid = false;
+  c->async_pending = true;
+  ctx_record_perf(c);
+  return LARA_OK;
 }
 
 }  // extern "C"

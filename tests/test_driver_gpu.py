@@ -250,3 +250,52 @@ def test_run_layer_composes_prologue_and_attention():
     gq, gk, gv = prologue.layer_prologue(pk(x), w_qkv, pk(g), q_pos_base=31, kv_pos_base=7)
     assert_bf16_parity(qw, gq, what="run_layer q")
     assert_bf16_parity(vw, gv, what="run_layer v")
+
+
+def test_async_decode_and_prefill_match_synchronous_calls():
+    """lara_decode / lara_prefill (stream-ordered, device buffers) + lara_sync give
+    the words of lara_run_query / lara_run_prefill_chunk."""
+    from lara_b200 import _native
+    from lara_b200.attn_driver import AttentionAccelerator
+
+    lib = _native.lib
+    rng = np.random.default_rng(13)
+    pk = oracle.fp32_to_bf16_u16
+    B, Hq, Hkv, D, L, n = 3, 32, 8, 128, 600, 40
+    k = pk(rng.standard_normal((B, Hkv, L, D)).astype(np.float32) * 0.5)
+    v = pk(rng.standard_normal((B, Hkv, L, D)).astype(np.float32) * 0.5)
+    q = pk(rng.standard_normal((B, Hq, D)).astype(np.float32) * 0.5)
+    qp = pk(rng.standard_normal((B, n, Hq, D)).astype(np.float32) * 0.5)
+    kn = pk(rng.standard_normal((B, Hkv, n, D)).astype(np.float32) * 0.5)
+    vn = pk(rng.standard_normal((B, Hkv, n, D)).astype(np.float32) * 0.5)
+    lens = np.array([500, 3, 250], np.int32)
+    dev = torch.device("cuda:0")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(dev)  # noqa: E731
+    stream = torch.cuda.Stream(device=dev)
+    with AttentionAccelerator() as sync_acc, AttentionAccelerator() as async_acc:
+        for acc in (sync_acc, async_acc):
+            acc.configure_heads(Hq, Hkv, D, max_seq_len=1024, batch=B)
+            acc.load_kv(k, v, lens)
+        want = sync_acc.run_query(q).copy()
+        qd = t(q)
+        torch.cuda.current_stream().synchronize()  # qd is written on torch's stream, read on `stream`
+        for splits in (0, 3):
+            od = torch.empty_like(qd)
+            _native.check(lib.lara_decode(async_acc._ctx, qd.data_ptr(), od.data_ptr(), splits, stream.cuda_stream),
+                          "lara_decode")
+            _native.check(lib.lara_sync(async_acc._ctx, 10_000), "lara_sync")
+            got = words_of(od)
+            if splits == 0:
+                np.testing.assert_array_equal(got, want)
+            else:
+                assert_bf16_parity(got, oracle.decode_attention(q, k, v, lens), what="lara_decode splits=3")
+        want_p = sync_acc.run_prefill_chunk(qp, kn, vn, causal=True)
+        # keep the device inputs referenced until lara_sync: the call is asynchronous
+        qpd, knd, vnd = t(qp), t(kn), t(vn)
+        op = torch.empty_like(qpd)
+        torch.cuda.current_stream().synchronize()  # the inputs are written on torch's stream
+        _native.check(lib.lara_prefill(async_acc._ctx, qpd.data_ptr(), knd.data_ptr(), vnd.data_ptr(),
+                                       op.data_ptr(), n, 1, stream.cuda_stream), "lara_prefill")
+        _native.check(lib.lara_sync(async_acc._ctx, 10_000), "lara_sync")
+        np.testing.assert_array_equal(words_of(op), want_p)
+        assert async_acc.seq_lens.tolist() == (lens + n).tolist()
