@@ -191,25 +191,46 @@ class CpuOracle:
         self.pool.shutdown()
 
 
-def cpu_decode_rate(q, k, v, lens, seconds: float, threads: int):
-    """Time the CPU oracle on whole decode steps until ``seconds`` have passed.
+def cpu_pass_times(q, k, v, lens, pairs, threads: int, repeats: int = 5, seconds: float = 0.0):
+    """One warm-up pass, then timed passes of the CPU oracle over ``pairs``.
 
-    Returns (GB/s, steps, elapsed)."""
-    B, Hkv = k.shape[0], k.shape[1]
-    pairs = [(b, h) for b in range(B) for h in range(Hkv)]
-    nbytes = int(np.sum(lens, dtype=np.int64)) * Hkv * k.shape[3] * 4
+    Passes are timed one by one with ``perf_counter_ns`` (the reference's
+    harness: 1 warm-up + 5 repeats, sw/board_performance.py:195-204); at least
+    ``repeats`` are taken, and more until ``seconds`` have passed.  Returns
+    (KV bytes per pass, list of pass seconds)."""
+    nbytes = sum(int(lens[b]) for b, _ in pairs) * k.shape[3] * 4
     runner = CpuOracle(q, k, v, lens, threads)
-    done, t0 = 0, time.perf_counter()
+    times = []
     try:
-        while True:
+        runner.step(pairs)
+        t_start = time.perf_counter()
+        while len(times) < repeats or time.perf_counter() - t_start < seconds:
+            t0 = time.perf_counter_ns()
             runner.step(pairs)
-            done += 1
-            el = time.perf_counter() - t0
-            if el >= seconds:
-                break
+            times.append((time.perf_counter_ns() - t0) * 1e-9)
     finally:
         runner.close()
-    return nbytes * done / el / 1e9, done, el
+    return nbytes, times
+
+
+def pass_stats(times) -> dict:
+    """min / median / p95 / max of pass times in seconds (sw/board_performance.py:321-331)."""
+    a = np.asarray(times, np.float64)
+    return {"repeats": int(a.size), "min_s": round(float(a.min()), 5), "median_s": round(float(np.median(a)), 5),
+            "p95_s": round(float(np.percentile(a, 95)), 5), "max_s": round(float(a.max()), 5)}
+
+
+def cpu_baseline_runs(q, k, v, lens, pairs, cores: int, seconds: float, one_thread_pass_s: float = 1.5):
+    """The oracle on all ``cores`` threads over ``pairs``, then on one thread over
+    a prefix of ``pairs`` sized for about ``one_thread_pass_s`` per pass.
+
+    Returns (all-core GB/s, its stats, one-thread GB/s, its stats, pairs in the one-thread sample)."""
+    nb, t_all = cpu_pass_times(q, k, v, lens, pairs, cores, 5, seconds)
+    st_all = pass_stats(t_all)
+    n1 = max(1, min(len(pairs), int(len(pairs) * one_thread_pass_s / max(st_all["median_s"] * cores, 1e-9))))
+    nb1, t_one = cpu_pass_times(q, k, v, lens, pairs[:n1], 1, 5)
+    st_one = pass_stats(t_one)
+    return nb / st_all["median_s"] / 1e9, st_all, nb1 / st_one["median_s"] / 1e9, st_one, n1
 
 
 # ---------------------------------------------------------------------------
@@ -253,12 +274,18 @@ def run_reference(args, rank: int, world: int) -> int:
     sample = all_pairs[:n_pairs]
     for _ in range(min(args.warmup, 3)):
         runner.step(sample)
-    t0 = time.perf_counter()
+    step_s = []
     for _ in range(args.steps):
+        t0 = time.perf_counter_ns()
         runner.step(sample)
-    t = (time.perf_counter() - t0) / max(args.steps, 1)
+        step_s.append((time.perf_counter_ns() - t0) * 1e-9)
+    t = sum(step_s) / max(args.steps, 1)
     runner.close()
     nbytes = n_pairs * L * D * 2 * 2
+    # the same harness on one thread (1 warm-up + 5 repeats over a smaller prefix)
+    n1 = max(1, min(n_pairs, int(n_pairs * 1.5 / max(t * cores, 1e-9))))
+    nb1, t_one = cpu_pass_times(q, k, v, lens, sample[:n1], 1, 5)
+    st_one = pass_stats(t_one)
     value = nbytes / t / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
@@ -270,7 +297,11 @@ def run_reference(args, rank: int, world: int) -> int:
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": f"{n_pairs} (sequence, kv-head) pairs x {L} tokens per step (of {B * Hkv}); the "
                                    f"reference's implementation of this path is CPU NumPy "
-                                   f"(sw/board_performance.py:158-192), run as the oracle port on {cores} threads"},
+                                   f"(sw/board_performance.py:158-192), run as the oracle port on {cores} threads",
+                         "pass_seconds": pass_stats(step_s),
+                         "single_thread": {"value": round(nb1 / st_one["median_s"] / 1e9, 3), "unit": "GB/s",
+                                           "cores": 1, "sample": f"first {n1} pairs of the same sample",
+                                           "pass_seconds": st_one}},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -510,10 +541,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         qn_, kn_, vn_ = (t[:nseq, :, :Ls].contiguous() if t.dim() == 4 else t[:nseq].contiguous()
                          for t in (q, k, v))
         qn_, kn_, vn_ = (t.view(torch.int16).cpu().numpy().view(np.uint16) for t in (qn_, kn_, vn_))
-        gbs, steps_done, el = cpu_decode_rate(qn_, kn_, vn_, lens_np[:nseq], args.cpu_seconds, cores)
+        pairs = [(b, h) for b in range(nseq) for h in range(cfg.n_kv_heads)]
+        gbs, st_all, gbs1, st_one, n1 = cpu_baseline_runs(qn_, kn_, vn_, lens_np[:nseq], pairs, cores,
+                                                          args.cpu_seconds)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-               "sample": f"{steps_done} pass(es) over {nseq} of {B} sequences ({int(lens_np[:nseq].sum())} tokens) "
-                         f"in {el:.1f} s; oracle restatement of sw/board_performance.py:158-192, {cores} threads"}
+               "sample": f"passes over {nseq} of {B} sequences ({int(lens_np[:nseq].sum())} tokens, "
+                         f"{len(pairs)} (sequence, kv-head) pairs) on {cores} threads, value from the median "
+                         f"pass; oracle restatement of sw/board_performance.py:158-192",
+               "pass_seconds": st_all,
+               "single_thread": {"value": round(gbs1, 3), "unit": "GB/s", "cores": 1,
+                                 "sample": f"first {n1} (sequence, kv-head) pairs of the same sample",
+                                 "pass_seconds": st_one}}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": S["scaling"],
