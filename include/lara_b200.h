@@ -87,6 +87,19 @@ LARA_API int lara_device_query(int device, lara_device_info* out);
 LARA_API int lara_decode_plan(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len,
                      const int32_t* lens_host, int* num_splits, int* chunk_tokens);
 
+/* Which decode kernel a geometry runs on: LARA_DECODE_KERNEL_TENSOR (the
+ * tcgen05 kernel: head_dim 128, groups of 8 or 16 query heads) or
+ * LARA_DECODE_KERNEL_CUDA_CORE.  The environment variable
+ * LARA_DECODE_PATH=simt|tc overrides the choice (tc also takes groups of 1, 2
+ * and 4).  The tensor-core kernel needs 16-byte aligned q/k/v rows and, for a
+ * paged cache, splits on 128-token boundaries (the planner's always are);
+ * otherwise the CUDA-core kernel runs.  Both give results within the parity
+ * bound of the same oracle, and a paged decode gives the same words as a
+ * contiguous one on the same kernel. */
+#define LARA_DECODE_KERNEL_CUDA_CORE 0
+#define LARA_DECODE_KERNEL_TENSOR 1
+LARA_API int lara_decode_kernel(int n_q_heads, int n_kv_heads, int head_dim);
+
 /* Bytes of device workspace a decode with `num_splits` splits needs. */
 LARA_API size_t lara_decode_workspace_bytes(int batch, int n_q_heads, int n_kv_heads, int head_dim, int num_splits);
 

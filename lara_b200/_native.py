@@ -28,6 +28,8 @@ LARA_ERR_DEVICE = 0x23
 
 LARA_ARITH_IEEE = 0
 LARA_ARITH_BOARD = 1
+LARA_DECODE_KERNEL_CUDA_CORE = 0
+LARA_DECODE_KERNEL_TENSOR = 1
 
 
 class LaraError(RuntimeError):
@@ -76,6 +78,7 @@ SIGNATURES = {
     "lara_device_query": (c_int, [c_int, POINTER(LaraDeviceInfo)]),
     "lara_decode_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, POINTER(c_int), POINTER(c_int)]),
     "lara_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "lara_decode_kernel": (c_int, [c_int, c_int, c_int]),
     "lara_workspace_init": (c_int, [c_void_p, c_size_t, c_void_p]),
     "lara_workspace_status": (c_int, [c_void_p, c_void_p, POINTER(c_int)]),
     "lara_gqa_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,

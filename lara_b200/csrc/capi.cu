@@ -51,9 +51,9 @@ int check_geometry(int batch, int hq, int hkv, int d, int lmax) {
     return fail(LARA_ERR_BAD_CFG, "geometry must be positive: batch=%d hq=%d hkv=%d d=%d lmax=%d", batch, hq, hkv,
                 d, lmax);
   if (hq % hkv != 0) return fail(LARA_ERR_BAD_CFG, "n_q_heads (%d) must be a multiple of n_kv_heads (%d)", hq, hkv);
-  if (lara::decode_tile_tokens(d, hq / hkv) == 0)
-    return fail(LARA_ERR_UNSUPPORTED, "no kernel compiled for head_dim=%d group=%d (supported: head_dim 64/128, "
-                "group 1, 2, 4, 8)", d, hq / hkv);
+  if (lara::decode_chunk_granule(d, hq / hkv) == 0)
+    return fail(LARA_ERR_UNSUPPORTED, "no kernel compiled for head_dim=%d group=%d (supported: head_dim 64/128 with "
+                "group 1, 2, 4, 8; head_dim 128 with group 16 on the tensor-core kernel)", d, hq / hkv);
   if (batch > 65535) return fail(LARA_ERR_BAD_CFG, "batch %d exceeds 65535", batch);
   return LARA_OK;
 }
@@ -73,7 +73,7 @@ struct DeviceGuard {
 
 int resolve_plan(int batch, int hq, int hkv, int d, int lmax, const int32_t* lens_host, int* nsplit, int* chunk) {
   if (*nsplit > 0 && *chunk > 0) {
-    const int tile = lara::decode_tile_tokens(d, hq / hkv);
+    const int tile = lara::decode_chunk_granule(d, hq / hkv);
     if (*chunk % tile != 0)
       return fail(LARA_ERR_BAD_CFG, "chunk_tokens (%d) must be a multiple of the kernel tile (%d)", *chunk, tile);
     if ((long long)*nsplit * *chunk < lmax)
@@ -340,6 +340,12 @@ int lara_decode_plan(int batch, int n_q_heads, int n_kv_heads, int head_dim, int
   if (!num_splits || !chunk_tokens) return fail(LARA_ERR_STREAM_DEST, "null output pointer");
   lara::decode_plan(batch, n_kv_heads, n_q_heads, head_dim, max_seq_len, lens_host, num_splits, chunk_tokens);
   return LARA_OK;
+}
+
+int lara_decode_kernel(int n_q_heads, int n_kv_heads, int head_dim) {
+  if (n_q_heads < 1 || n_kv_heads < 1 || n_q_heads % n_kv_heads) return LARA_DECODE_KERNEL_CUDA_CORE;
+  return lara::decode_tc_selected(head_dim, n_q_heads / n_kv_heads) ? LARA_DECODE_KERNEL_TENSOR
+                                                                     : LARA_DECODE_KERNEL_CUDA_CORE;
 }
 
 size_t lara_decode_workspace_bytes(int batch, int n_q_heads, int n_kv_heads, int head_dim, int num_splits) {
@@ -1141,7 +1147,7 @@ int lara_decode(lara_ctx* c, const uint16_t* q, uint16_t* o, int splits, void* s
   const cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
   int ns = 0, ch = 0;
   if (splits > 0) {
-    const int tile = lara::decode_tile_tokens(c->d, c->hq / c->hkv);
+    const int tile = lara::decode_chunk_granule(c->d, c->hq / c->hkv);
     ch = ((c->lmax + splits - 1) / splits + tile - 1) / tile * tile;
     ns = (c->lmax + ch - 1) / ch;
   } else {

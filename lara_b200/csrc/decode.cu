@@ -38,6 +38,7 @@
 #include <utility>
 
 #include "common.cuh"
+#include "decode_merge.cuh"
 #include "lara_internal.h"
 
 namespace lara {
@@ -475,32 +476,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   __syncthreads();
   if (!flag[1]) return;
   __threadfence();
-  for (int idx = tid; idx < G * D / 2; idx += T::kThreads) {
-    const int g = idx / (D / 2);
-    const int d = (idx % (D / 2)) * 2;
-    const int h = kvh * G + g;
-    const long long row = (long long)b * p.n_q_heads + h;
-    const float* ml = p.part_ml + row * p.nsplit * 2;
-    const float* pa = p.part_acc + row * p.nsplit * D;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < nsplit_b; ++s2) M = fmaxf(M, __ldcg(ml + s2 * 2));
-    const float Mu = (M == -INFINITY) ? 0.f : M;
-    float L = 0.f, o0 = 0.f, o1 = 0.f;
-    for (int s2 = 0; s2 < nsplit_b; ++s2) {
-      const float sc = exp2f(__ldcg(ml + s2 * 2) - Mu);
-      L = fmaf(__ldcg(ml + s2 * 2 + 1), sc, L);
-      const float2 a = __ldcg(reinterpret_cast<const float2*>(pa + (long long)s2 * D + d));
-      o0 = fmaf(a.x, sc, o0);
-      o1 = fmaf(a.y, sc, o1);
-    }
-    if (partial_out) {
-      *reinterpret_cast<float2*>(p.out_acc + row * D + d) = make_float2(o0, o1);
-      if (d == 0) { p.out_ml[row * 2] = M; p.out_ml[row * 2 + 1] = L; }
-    } else {
-      const float inv = (L > 0.f) ? 1.f / L : 0.f;
-      *reinterpret_cast<uint32_t*>(p.o + b * p.o_sb + h * p.o_sh + d) = pack2_bf16(o0 * inv, o1 * inv);
-    }
-  }
+  merge_split_partials<D>(p, b, kvh, G, nsplit_b, partial_out, tid, T::kThreads);
 }
 
 // ---------------------------------------------------------------------------
@@ -556,6 +532,12 @@ int device_sm_count() {
 
 int decode_tile_tokens(int head_dim, int group) { return lookup(head_dim, group).tile; }
 
+int decode_chunk_granule(int head_dim, int group) {
+  const int tile = decode_tile_tokens(head_dim, group);
+  if (tile > 0) return tile;
+  return decode_tc_selected(head_dim, group) ? 128 : 0;
+}
+
 WorkspaceLayout decode_workspace_layout(int batch, int n_q_heads, int n_kv_heads, int head_dim, int nsplit) {
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   WorkspaceLayout w;
@@ -571,6 +553,10 @@ WorkspaceLayout decode_workspace_layout(int batch, int n_q_heads, int n_kv_heads
 void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max_tokens, const int32_t* lens_host,
                  int* nsplit_out, int* chunk_out) {
   const int group = n_kv_heads > 0 ? n_q_heads / n_kv_heads : 1;
+  if (decode_tc_selected(head_dim, group)) {
+    decode_tc_plan(batch, n_kv_heads, max_tokens, lens_host, nsplit_out, chunk_out);
+    return;
+  }
   const KernelInfo k = lookup(head_dim, group);
   const int tile = k.tile > 0 ? k.tile : 64;
   const int L = max_tokens < 1 ? 1 : max_tokens;
@@ -625,7 +611,7 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
 }
 
 int decode_first_chunk(int nsplit, int chunk, int group, int head_dim) {
-  if (nsplit != 2) return 0;
+  if (nsplit != 2 || decode_tc_selected(head_dim, group)) return 0;
   const int tile = decode_tile_tokens(head_dim, group);
   if (tile <= 0) return 0;
   const long long span = 2ll * chunk;
@@ -635,6 +621,10 @@ int decode_first_chunk(int nsplit, int chunk, int group, int head_dim) {
 
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream) {
   const int group = p.n_q_heads / p.n_kv_heads;
+  if (decode_tc_selected(p.head_dim, group)) {
+    const cudaError_t e = decode_tc_launch(p, stream);
+    if (e != cudaErrorNotSupported) return e;
+  }
   const KernelInfo k = lookup(p.head_dim, group);
   if (!k.fn) return cudaErrorInvalidValue;
   if (p.chunk <= 0 || p.chunk % k.tile != 0 || p.nsplit <= 0) return cudaErrorInvalidValue;

@@ -1,0 +1,765 @@
+// GQA decode attention on the 5th-generation tensor cores (tcgen05 + TMEM,
+// sm_100a): a persistent kernel for head_dim 128 and groups of up to 16
+// query heads per KV head.
+//
+// Same contract as the CUDA-core decode kernel (DecodeParams: query rows,
+// per-row lengths, splits of `chunk` tokens, bf16 output or (m, l, acc)
+// partials, last-arriver split merge), and the same arithmetic as the
+// reference datapath (hw/rtl/attn_top.sv:301-625: QK^T, scale, online
+// softmax per block, P.V, O = O*corr + dO, normalise by l).  The G query
+// heads of a KV group are the N = 16 columns of two small MMAs per tile of
+// 128 cached tokens:
+//
+//   S^T [128 tokens x 16]   = K_tile [128 x 128] . Q^T      A = K (K-major), B = Q (K-major)
+//   O^T [128 dims x 16]     = V_tile^T [128 x 128] . P^T    A = V (MN-major), B = P^T (K-major)
+//
+// so the group's FLOPs (8 per cached byte at G = 8) leave the CUDA cores and
+// the SM only streams K/V.  P is split as P_hi + P_lo (two bf16 terms, ~16
+// significant bits) for a second PV pass, so the result keeps the accuracy
+// of an fp32 P.
+//
+// One CTA per SM, 6 warps:
+//   warp 4 (TMA)   takes work items (query row, kv head, split) from a ticket
+//                  counter in the workspace and streams each item's Q (once)
+//                  and K/V tiles back to back through a 3-stage ring of
+//                  64 KB stages (tensor-map copies, 128-byte swizzle, L2
+//                  evict-first, no multicast).  Each stage carries a small
+//                  descriptor of its tile (row, head, token range, item
+//                  boundaries); items without tokens travel as marker stages.
+//   warp 5 (MMA)   one thread issues S(n+1) before PV(n), so the softmax of
+//                  one tile overlaps the tensor core's work on the next.
+//   warps 0-3      TMEM lane t: token t of a tile for the softmax (scale,
+//                  length mask, per-head tile max by redux.sync and a 4-warp
+//                  exchange, exp2, P_hi/P_lo into shared memory), and head
+//                  dim t of the output (O^T of each tile added into registers
+//                  with the online-softmax correction).  At an item's end the
+//                  row sums are reduced and the item's output or split
+//                  partial is written; the last split to finish merges.
+//
+// TMEM: S^T in columns [0, 32) (two buffers of 16), O^T in [32, 64).
+// Every wait is bounded by %globaltimer (the 128 softmax threads also meet on
+// an mbarrier rather than bar.sync); on a timeout the CTA flags the status
+// word, drains its own tensor-core work and copies, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+#include "decode_merge.cuh"
+#include "lara_internal.h"
+#include "tcgen05.cuh"
+
+namespace lara {
+
+using namespace tc;
+
+namespace {
+
+constexpr int kD = 128;                  // head_dim
+constexpr int kTile = 128;               // tokens per tile (TMEM lanes of S^T)
+constexpr int kN = 16;                   // MMA N: query heads of the group, padded
+constexpr int kHalf = kTile * 128;       // [128 rows][64 bf16] with 128-byte swizzle
+constexpr int kKVBytes = 2 * kHalf;      // one K (or V) tile
+constexpr int kStages = 3;
+constexpr int kOpBytes = 2 * kN * 128;   // [2 k-blocks][16 rows][128 B]: Q, or one of P_hi / P_lo
+constexpr int kKOff = 0;
+constexpr int kVOff = kKOff + kStages * kKVBytes;
+constexpr int kQOff = kVOff + kStages * kKVBytes;   // two item buffers
+constexpr int kPOff = kQOff + 2 * kOpBytes;         // two tile buffers x (P_hi, P_lo)
+constexpr int kXOff = kPOff + 4 * kOpBytes;         // exchange: tile max [2][4][16], row sums [4][16], flag
+constexpr int kMetaOff = kXOff + 1024;
+constexpr int kBarOff = kMetaOff + 256;
+constexpr int kSmemAlloc = kBarOff + 256 + 1024;    // + slack for 1024-byte alignment
+constexpr uint32_t kTmemCols = 64;
+constexpr int kTmaWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kThreads = 6 * 32;
+constexpr unsigned kFull = 0xffffffffu;
+
+enum : int { kEntryTile = 0, kEntryZero = 1, kEntryEnd = 2 };
+
+// One ring stage's work, written by the producer before it arrives on the
+// stage's full barrier.
+struct Meta {
+  int kind;      // kEntryTile, kEntryZero (a row with no visible key), kEntryEnd
+  int row;       // query row
+  int kvh;
+  int split;
+  int tok0;      // first token of the tile
+  int tok_end;   // end of the item's tokens
+  int nsplit_b;  // splits that hold tokens of this row
+  int flags;     // bit 0: first tile of its item, bit 1: last tile
+  int seq_kv;    // K/V sequence coordinate of the tensor maps
+  int qslot;     // Q buffer of the item
+  int qpar;      // phase parity of that buffer's load
+  int pad[5];
+};
+static_assert(sizeof(Meta) == 64 && kStages * sizeof(Meta) <= 256, "stage descriptors");
+
+struct Bars {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t q_full[2];
+  uint64_t q_free[2];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_full[2];
+  uint64_t sync;   // the 128 softmax threads
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int issued;      // ring entries pushed
+  int q_issued;    // Q loads issued
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+struct TcDecodeArgs {
+  unsigned n_items;  // nsplit * batch * n_kv_heads
+  int kv_shared;     // every row reads K/V sequence 0 (kv_sb == 0)
+  int q_rows;        // rows of the Q box (min(16, n_q_heads))
+  int page_box;      // paged cache: token rows per copy (min(128, page size)); 0 = contiguous cache
+};
+
+__device__ __forceinline__ float warp_max(float x) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ int row_len(const DecodeParams& p, int seq, int row_in_seq) {
+  long long len = (long long)p.len_c0 + (long long)p.len_c1 * row_in_seq;
+  if (p.lens) {
+    const int l = p.lens[seq];
+    if (l < 0 || l > p.max_seq_len) atomicOr(p.status, kDevBadLength);
+    len += l;
+  }
+  return len < 0 ? 0 : (len > p.max_seq_len ? p.max_seq_len : (int)len);
+}
+
+// 128-thread meeting point of the softmax warps on an mbarrier (bounded).
+__device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, volatile int* abort) {
+  mbar_arrive(bar);
+  const bool ok = wait_or_abort(bar, phase & 1, abort);
+  ++phase;
+  return __all_sync(kFull, ok);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1)
+    gqa_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const DecodeParams p, const TcDecodeArgs a) {
+  constexpr int NC = G <= 8 ? 8 : 16;  // TMEM columns read per lane
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + kBarOff);
+  Meta* metas = reinterpret_cast<Meta*>(smem + kMetaOff);
+  volatile int* abort = &bars->abort;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  unsigned* queue = reinterpret_cast<unsigned*>(p.status + 32);  // [0] ticket, [1] finished CTAs
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->q_full[i], 1);
+      mbar_init(&bars->q_free[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], 128);
+      mbar_init(&bars->o_full[i], 1);
+    }
+    mbar_init(&bars->sync, 128);
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    bars->issued = 0;
+    bars->q_issued = 0;
+    mbar_fence_init();
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&bars->tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x < 128) {
+    // P^T rows >= G stay zero for the whole kernel, so padded heads add nothing
+    uint4* pz = reinterpret_cast<uint4*>(smem + kPOff) + threadIdx.x * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pz[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == kTmaWarp) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = make_evict_first_policy();
+      const int per_split = p.batch * p.n_kv_heads;
+      const int c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
+      const uint32_t q_bytes = 2u * 128u * (uint32_t)a.q_rows;
+      int n = 0, qi = 0;
+      auto push = [&](const Meta& m, bool copies) -> bool {
+        const int st = n % kStages;
+        if (n >= kStages && !wait_or_abort(&bars->empty[st], ((n / kStages) - 1) & 1, abort)) return false;
+        metas[st] = m;
+        if (copies && a.page_box == 0) {
+          uint8_t* ks = smem + kKOff + st * kKVBytes;
+          uint8_t* vs = smem + kVOff + st * kKVBytes;
+          mbar_arrive_expect_tx(&bars->full[st], 2 * kKVBytes);
+          tma_load_4d_hint(ks, &tm_k, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+          tma_load_4d_hint(ks + kHalf, &tm_k, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+          tma_load_4d_hint(vs, &tm_v, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+          tma_load_4d_hint(vs + kHalf, &tm_v, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+        } else if (copies) {
+          // paged cache: the tile is page_box-row pieces of whole pages (tiles
+          // start on 128-token boundaries); pieces past the item's end are not
+          // loaded (their rows are masked, and V rows zeroed, by the softmax)
+          uint8_t* ks = smem + kKOff + st * kKVBytes;
+          uint8_t* vs = smem + kVOff + st * kKVBytes;
+          const int bx = a.page_box;
+          const int pieces = min(kTile / bx, (m.tok_end - m.tok0 + bx - 1) / bx);
+          int pages[kTile / 16];
+          const int32_t* row = p.block_table + (long long)m.seq_kv * p.pages_per_seq;
+#pragma unroll
+          for (int i = 0; i < kTile / 16; ++i) {
+            if (i < pieces) {
+              int pg = __ldg(row + ((m.tok0 + i * bx) >> p.page_log2));
+              if (pg < 0 || pg >= p.num_pages) {
+                atomicOr(p.status, kDevBadPage);
+                pg = 0;  // keep every copy in bounds
+              }
+              pages[i] = pg;
+            }
+          }
+          mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
+          const int ps_mask = (1 << p.page_log2) - 1;
+#pragma unroll
+          for (int i = 0; i < kTile / 16; ++i) {
+            if (i < pieces) {
+              const int in_page = (m.tok0 + i * bx) & ps_mask;
+              const int off = i * bx * 128;
+              tma_load_4d_hint(ks + off, &tm_k, 0, in_page, m.kvh, pages[i], &bars->full[st], pol);
+              tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, in_page, m.kvh, pages[i], &bars->full[st], pol);
+              tma_load_4d_hint(vs + off, &tm_v, 0, in_page, m.kvh, pages[i], &bars->full[st], pol);
+              tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, in_page, m.kvh, pages[i], &bars->full[st], pol);
+            }
+          }
+        } else {
+          mbar_arrive(&bars->full[st]);
+        }
+        bars->issued = ++n;
+        return true;
+      };
+      bool ok = true;
+      while (ok) {
+        const unsigned item = atomicAdd(queue, 1u);
+        Meta m{};
+        if (item >= a.n_items) {
+          m.kind = kEntryEnd;
+          (void)push(m, false);
+          break;
+        }
+        const int split = (int)(item / (unsigned)per_split);
+        const int rem = (int)(item - (unsigned)split * (unsigned)per_split);
+        const int b = rem / p.n_kv_heads;
+        const int kvh = rem - b * p.n_kv_heads;
+        const int seq = b / p.rows_per_seq;
+        const int len = row_len(p, seq, b - seq * p.rows_per_seq);
+        const int tok_begin = split == 0 ? 0 : c0 + (split - 1) * p.chunk;
+        m.row = b;
+        m.kvh = kvh;
+        m.split = split;
+        if (len == 0) {
+          // no visible key: split 0 writes the zero output (the RTL normaliser maps l == 0 to 0)
+          if (split != 0) continue;
+          m.kind = kEntryZero;
+          ok = push(m, false);
+          continue;
+        }
+        if (tok_begin >= len) continue;
+        const int ntok = min(len - tok_begin, split == 0 ? c0 : p.chunk);
+        m.kind = kEntryTile;
+        m.tok_end = tok_begin + ntok;
+        m.nsplit_b = len <= c0 ? 1 : 1 + (len - c0 + p.chunk - 1) / p.chunk;
+        m.seq_kv = a.kv_shared ? 0 : seq;
+        // the item's query heads (rows past the group are never used)
+        const int qs = qi & 1;
+        if (qi >= 2 && !wait_or_abort(&bars->q_free[qs], ((qi - 2) >> 1) & 1, abort)) break;
+        uint8_t* qd = smem + kQOff + qs * kOpBytes;
+        mbar_arrive_expect_tx(&bars->q_full[qs], q_bytes);
+        tma_load_3d(qd, &tm_q, 0, kvh * G, b, &bars->q_full[qs]);
+        tma_load_3d(qd + kOpBytes / 2, &tm_q, 64, kvh * G, b, &bars->q_full[qs]);
+        m.qslot = qs;
+        m.qpar = (qi >> 1) & 1;
+        bars->q_issued = ++qi;
+        const int ntiles = (ntok + kTile - 1) / kTile;
+        for (int j = 0; ok && j < ntiles; ++j) {
+          m.tok0 = tok_begin + j * kTile;
+          m.flags = (j == 0 ? 1 : 0) | (j == ntiles - 1 ? 2 : 0);
+          ok = push(m, true);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16(kTile, kN, 0, 0);
+      const uint32_t id_pv = idesc_bf16(kD, kN, 0, 1);
+      auto issue_s = [&](int n, const Meta& m) -> bool {
+        const int slot = n & 1;
+        if (m.kind != kEntryTile) {
+          mbar_arrive(&bars->s_full[slot]);
+          return true;
+        }
+        if ((m.flags & 1) && !wait_or_abort(&bars->q_full[m.qslot], m.qpar, abort)) return false;
+        tc_fence_after();
+        const uint32_t k_base = smem_addr(smem + kKOff + (n % kStages) * kKVBytes);
+        const uint32_t q_base = smem_addr(smem + kQOff + m.qslot * kOpBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ka = k_base + (kk >> 2) * kHalf + (kk & 3) * 32;
+          const uint32_t qa = q_base + (kk >> 2) * (kOpBytes / 2) + (kk & 3) * 32;
+          mma_ss(tmem + slot * kN, desc_sw128(ka, 16, 1024), desc_sw128(qa, 16, 1024), id_s, kk > 0);
+        }
+        mma_commit(&bars->s_full[slot]);
+        if (m.flags & 2) mma_commit(&bars->q_free[m.qslot]);
+        return true;
+      };
+      int n = 0;
+      Meta cur{};
+      bool ok = wait_or_abort(&bars->full[0], 0, abort);
+      if (ok) {
+        cur = metas[0];
+        ok = issue_s(0, cur);
+      }
+      while (ok) {
+        const bool more = cur.kind != kEntryEnd;
+        Meta nxt{};
+        if (more) {
+          const int s1 = (n + 1) % kStages;
+          if (!wait_or_abort(&bars->full[s1], ((n + 1) / kStages) & 1, abort)) break;
+          nxt = metas[s1];
+          if (!issue_s(n + 1, nxt)) break;
+        }
+        const int slot = n & 1;
+        const int st = n % kStages;
+        if (!wait_or_abort(&bars->p_full[slot], (n >> 1) & 1, abort)) break;
+        tc_fence_after();
+        if (cur.kind == kEntryTile) {
+          const uint32_t v_base = smem_addr(smem + kVOff + st * kKVBytes);
+          const uint32_t ph = smem_addr(smem + kPOff + slot * 2 * kOpBytes);
+#pragma unroll
+          for (int part = 0; part < 2; ++part) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t va = v_base + kk * 16 * 128;
+              const uint32_t pa = ph + part * kOpBytes + (kk >> 2) * (kOpBytes / 2) + (kk & 3) * 32;
+              mma_ss(tmem + 32 + slot * kN, desc_sw128(va, kHalf, 1024), desc_sw128(pa, 16, 1024), id_pv,
+                     (part | kk) > 0);
+            }
+          }
+          mma_commit(&bars->o_full[slot]);
+          mma_commit(&bars->empty[st]);
+        } else {
+          mbar_arrive(&bars->o_full[slot]);
+          mbar_arrive(&bars->empty[st]);
+        }
+        if (!more) break;
+        cur = nxt;
+        ++n;
+      }
+      mma_commit(&bars->drain);
+      (void)mbar_wait_bounded(&bars->drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int t = threadIdx.x;  // token of a tile (S^T lane) and head dim (O^T lane)
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    float* xmax = reinterpret_cast<float*>(smem + kXOff);  // [2][4][16]
+    float* lsum = xmax + 2 * 4 * 16;                        // [4][16]
+    volatile int* bcast = reinterpret_cast<volatile int*>(lsum + 4 * 16);
+    const bool partial_out = p.out_acc != nullptr;
+    uint32_t sync_phase = 0;
+    int xpar = 0;
+    float m_run[G], l_part[G], o_acc[G], alpha_prev[G], alpha_cur[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m_run[g] = -INFINITY;
+      l_part[g] = 0.f;
+      o_acc[g] = 0.f;
+      alpha_prev[g] = 1.f;
+      alpha_cur[g] = 1.f;
+    }
+    // P^T element (head g, token t) in the 128-byte-swizzled K-major layout
+    const int p_off = (t >> 6) * (kOpBytes / 2) + (t & 7) * 2;
+    const int p_chunk = (t & 63) >> 3;
+
+    auto accumulate = [&](int n) -> bool {  // o_acc = o_acc * alpha + O^T(n)
+      if (!__all_sync(kFull, wait_or_abort(&bars->o_full[n & 1], (n >> 1) & 1, abort))) return false;
+      tc_fence_after();
+      float ov[NC];
+      if constexpr (NC == 8) tmem_ld8(lane_base + 32 + (n & 1) * kN, ov);
+      else tmem_ld16(lane_base + 32 + (n & 1) * kN, ov);
+      tmem_wait_ld();
+#pragma unroll
+      for (int g = 0; g < G; ++g) o_acc[g] = fmaf(o_acc[g], alpha_prev[g], ov[g]);
+      tc_fence_before();
+      return true;
+    };
+
+    auto epilogue = [&](const Meta& m) -> bool {
+      float L[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float v = l_part[g];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off);
+        L[g] = v;
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) lsum[warp * 16 + g] = L[g];
+      }
+      if (!group_sync(&bars->sync, sync_phase, abort)) return false;
+#pragma unroll
+      for (int g = 0; g < G; ++g) L[g] = (lsum[g] + lsum[16 + g]) + (lsum[32 + g] + lsum[48 + g]);
+      const int b = m.row, kvh = m.kvh;
+      if (m.nsplit_b == 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const int h = kvh * G + g;
+          const long long row = (long long)b * p.n_q_heads + h;
+          if (partial_out) {
+            p.out_acc[row * kD + t] = o_acc[g];
+            if (t == 0) { p.out_ml[row * 2] = m_run[g]; p.out_ml[row * 2 + 1] = L[g]; }
+          } else {
+            const float inv = (L[g] > 0.f) ? 1.f / L[g] : 0.f;
+            p.o[b * p.o_sb + h * p.o_sh + t] = (uint16_t)f32_to_bf16_rne_bits(o_acc[g] * inv);
+          }
+        }
+        return true;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const long long slot = ((long long)b * p.n_q_heads + kvh * G + g) * p.nsplit + m.split;
+        p.part_acc[slot * kD + t] = o_acc[g];
+        if (t == 0) { p.part_ml[slot * 2] = m_run[g]; p.part_ml[slot * 2 + 1] = L[g]; }
+      }
+      __threadfence();
+      if (!group_sync(&bars->sync, sync_phase, abort)) return false;
+      if (t == 0) {
+        int* ctr = p.counters + b * p.n_kv_heads + kvh;
+        const int prev = atomicAdd(ctr, 1);
+        const int last = (prev == m.nsplit_b - 1);
+        if (last) *ctr = 0;  // every other split has arrived: reset for the next launch
+        *bcast = last;
+      }
+      if (!group_sync(&bars->sync, sync_phase, abort)) return false;
+      if (*bcast) {
+        __threadfence();
+        merge_split_partials<kD>(p, b, kvh, G, m.nsplit_b, partial_out, t, 128);
+      }
+      return true;
+    };
+
+    auto softmax_tile = [&](int n, const Meta& m) -> bool {
+      const int slot = n & 1;
+      float sv[NC];
+      if constexpr (NC == 8) tmem_ld8(lane_base + slot * kN, sv);
+      else tmem_ld16(lane_base + slot * kN, sv);
+      tmem_wait_ld();
+      const bool valid = m.tok0 + t < m.tok_end;
+      float* xb = xmax + xpar * 64;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        sv[g] = valid ? sv[g] * p.scale_log2 : -INFINITY;
+        const float wm = warp_max(sv[g]);
+        if (lane == 0) xb[warp * 16 + g] = wm;
+      }
+      if (!valid) {
+        // keys past the item's end carry p = 0; zero their V rows so stale
+        // cache contents (NaN, Inf) cannot reach the P.V sum
+        uint4* v0 = reinterpret_cast<uint4*>(smem + kVOff + (n % kStages) * kKVBytes + t * 128);
+        uint4* v1 = reinterpret_cast<uint4*>(smem + kVOff + (n % kStages) * kKVBytes + kHalf + t * 128);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v0[i] = make_uint4(0, 0, 0, 0);
+          v1[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      if (!group_sync(&bars->sync, sync_phase, abort)) return false;
+      uint8_t* ph = smem + kPOff + slot * 2 * kOpBytes;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float tmax = fmaxf(fmaxf(xb[g], xb[16 + g]), fmaxf(xb[32 + g], xb[48 + g]));
+        const float m_new = fmaxf(m_run[g], tmax);
+        alpha_cur[g] = (m_new == m_run[g]) ? 1.f : exp2f(m_run[g] - m_new);
+        m_run[g] = m_new;
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        const float pr = exp2f(sv[g] - m_use);
+        l_part[g] = fmaf(l_part[g], alpha_cur[g], pr);
+        // pr - bf16(pr) is exact in fp32; its bf16 rounding carries the next 8 bits
+        const __nv_bfloat16 hb = __float2bfloat16_rn(pr);
+        const __nv_bfloat16 lb = __float2bfloat16_rn(pr - __bfloat162float(hb));
+        const int off = p_off + g * 128 + ((p_chunk ^ (g & 7)) << 4);
+        *reinterpret_cast<__nv_bfloat16*>(ph + off) = hb;
+        *reinterpret_cast<__nv_bfloat16*>(ph + kOpBytes + off) = lb;
+      }
+      xpar ^= 1;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[slot]);
+      return true;
+    };
+
+    bool pending = false;  // O^T of the previous entry (a tile) not yet added
+    Meta item{};
+    for (int n = 0;; ++n) {
+      const int st = n % kStages;
+      if (!__all_sync(kFull, wait_or_abort(&bars->full[st], (n / kStages) & 1, abort))) break;
+      const Meta m = metas[st];
+      const bool cont = m.kind == kEntryTile && !(m.flags & 1);
+      if (pending && !cont) {
+        // the previous item ended with tile n-1: finish it first
+        if (!accumulate(n - 1) || !epilogue(item)) break;
+        pending = false;
+      }
+      if (m.kind == kEntryTile && (m.flags & 1)) {
+        item = m;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          m_run[g] = -INFINITY;
+          l_part[g] = 0.f;
+          o_acc[g] = 0.f;
+        }
+      }
+      if (!__all_sync(kFull, wait_or_abort(&bars->s_full[n & 1], (n >> 1) & 1, abort))) break;
+      tc_fence_after();
+      if (m.kind == kEntryTile) {
+        if (!softmax_tile(n, m)) break;
+      } else {
+        tc_fence_before();
+        mbar_arrive(&bars->p_full[n & 1]);
+      }
+      if (pending && !accumulate(n - 1)) break;
+      if (m.kind == kEntryTile) {
+        pending = true;
+#pragma unroll
+        for (int g = 0; g < G; ++g) alpha_prev[g] = alpha_cur[g];
+      } else if (m.kind == kEntryZero) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const int h = m.kvh * G + g;
+          const long long row = (long long)m.row * p.n_q_heads + h;
+          if (partial_out) {
+            p.out_acc[row * kD + t] = 0.f;
+            if (t == 0) { p.out_ml[row * 2] = -INFINITY; p.out_ml[row * 2 + 1] = 0.f; }
+          } else {
+            p.o[m.row * p.o_sb + h * p.o_sh + t] = 0;
+          }
+        }
+      } else {
+        break;  // end of work
+      }
+    }
+  }
+
+  // ------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (*abort) {
+    if (threadIdx.x == 0) atomicOr(p.status, kDevWaitTimeout);
+    if (threadIdx.x == kTmaWarp * 32) {
+      // let this CTA's own copies land before its shared memory is released
+      const int issued = bars->issued;
+      for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)
+        (void)mbar_wait_bounded(&bars->full[j % kStages], (j / kStages) & 1);
+      const int qn = bars->q_issued;
+      for (int j = (qn > 2 ? qn - 2 : 0); j < qn; ++j) (void)mbar_wait_bounded(&bars->q_full[j & 1], (j >> 1) & 1);
+    }
+  }
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+  if (threadIdx.x == 0) {
+    // the last CTA to finish resets the work queue for the next launch
+    __threadfence();
+    if (atomicAdd(queue + 1, 1u) == gridDim.x - 1) {
+      queue[0] = 0;
+      queue[1] = 0;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+enum class DecodePath { kAuto, kSimt, kTensor };
+
+DecodePath path_override() {
+  const char* e = std::getenv("LARA_DECODE_PATH");
+  if (!e) return DecodePath::kAuto;
+  if (std::strcmp(e, "simt") == 0) return DecodePath::kSimt;
+  if (std::strcmp(e, "tc") == 0) return DecodePath::kTensor;
+  return DecodePath::kAuto;
+}
+
+// Groups at or above this size run on the tensor cores by default.  Below it
+// the CUDA-core kernel streams K/V at the HBM rate already.
+constexpr int kAutoMinGroup = 8;
+
+const void* kernel_for(int group) {
+  switch (group) {
+    case 1: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<1>);
+    case 2: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<2>);
+    case 4: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<4>);
+    case 8: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<8>);
+    case 16: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<16>);
+    default: return nullptr;
+  }
+}
+
+bool stride_ok(long long elems) { return elems > 0 && (elems * 2) % 16 == 0 && elems * 2 < (1ll << 40); }
+
+}  // namespace
+
+bool decode_tc_selected(int head_dim, int group) {
+  const DecodePath path = path_override();
+  if (path == DecodePath::kSimt) return false;
+  if (head_dim != kD || kernel_for(group) == nullptr || !tensor_maps_available()) return false;
+  return path == DecodePath::kTensor || group >= kAutoMinGroup;
+}
+
+void decode_tc_plan(int batch, int n_kv_heads, int max_tokens, const int32_t* lens_host, int* nsplit_out,
+                    int* chunk_out) {
+  // Items are dispensed one by one to resident CTAs (one per SM), so the step
+  // takes about (total tiles + per-item overhead) / SMs plus the last item.
+  constexpr double kItemOverhead = 0.35;  // tiles of stream time an item costs beyond its own tiles
+  const double sms = device_sm_count();
+  const int L = max_tokens < 1 ? 1 : max_tokens;
+  const int max_tiles = (L + kTile - 1) / kTile;
+  double best = 1e300;
+  int best_chunk = max_tiles * kTile, best_s = 1;
+  for (long long chunk = kTile;; chunk *= 2) {
+    if (chunk > (long long)max_tiles * kTile) chunk = (long long)max_tiles * kTile;
+    const int c = (int)chunk;
+    double tiles = 0.0, items = 0.0;
+    long long longest = 0;
+    for (int b = 0; b < (lens_host ? batch : 1); ++b) {
+      const int len = lens_host ? (lens_host[b] < 0 ? 0 : (lens_host[b] > L ? L : lens_host[b])) : L;
+      if (len == 0) {
+        items += 1;
+        continue;
+      }
+      const int ns = (len + c - 1) / c;
+      const int last = len - (ns - 1) * c;
+      tiles += (double)(ns - 1) * (c / kTile) + (double)((last + kTile - 1) / kTile);
+      items += ns;
+      const long long first = len < c ? len : c;
+      if (first > longest) longest = first;
+    }
+    if (!lens_host) {
+      tiles *= batch;
+      items *= batch;
+    }
+    tiles *= n_kv_heads;
+    items *= n_kv_heads;
+    const double per_item = (double)((longest + kTile - 1) / kTile) + kItemOverhead;
+    double cost;
+    if (!lens_host) {
+      // equal items: whole waves of them
+      cost = std::ceil(items / sms) * per_item;
+    } else {
+      cost = (tiles + items * kItemOverhead) / sms + per_item;
+    }
+    if (cost < best * (1.0 - 1e-9)) {
+      best = cost;
+      best_chunk = c;
+      best_s = (L + c - 1) / c;
+    }
+    if (c >= max_tiles * kTile) break;
+  }
+  *nsplit_out = best_s;
+  *chunk_out = best_chunk;
+}
+
+cudaError_t decode_tc_launch(const DecodeParams& p, cudaStream_t stream) {
+  const int group = p.n_kv_heads > 0 ? p.n_q_heads / p.n_kv_heads : 0;
+  const void* fn = kernel_for(group);
+  if (!fn || p.head_dim != kD) return cudaErrorNotSupported;
+  const bool paged = p.block_table != nullptr;
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (!al16(p.q) || !al16(p.k) || !al16(p.v) || !stride_ok(p.q_sh)) return cudaErrorNotSupported;
+  if (p.batch > 1 && !stride_ok(p.q_sb)) return cudaErrorNotSupported;
+  const bool kv_shared = !paged && p.kv_sb == 0;
+  const long long nseq_kv = kv_shared ? 1 : (p.batch + p.rows_per_seq - 1) / p.rows_per_seq;
+  if (!paged && !stride_ok(p.kv_sh)) return cudaErrorNotSupported;
+  if (!paged && !kv_shared && nseq_kv > 1 && !stride_ok(p.kv_sb)) return cudaErrorNotSupported;
+  // a paged tile is whole pieces of pages: splits start on 128-token boundaries
+  if (paged && (p.chunk % kTile != 0 || p.chunk0 % kTile != 0 || p.page_log2 < 4)) return cudaErrorNotSupported;
+  if (p.chunk <= 0 || p.nsplit <= 0 || p.chunk0 < 0 || p.rows_per_seq < 1) return cudaErrorInvalidValue;
+  const long long c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
+  if (c0 + (long long)(p.nsplit - 1) * p.chunk < (long long)p.max_seq_len) return cudaErrorInvalidValue;
+  const long long n_items = (long long)p.nsplit * p.batch * p.n_kv_heads;
+  if (n_items >= (1ll << 31)) return cudaErrorInvalidValue;
+
+  const int q_rows = p.n_q_heads < kN ? p.n_q_heads : kN;
+  CUtensorMap mq, mk, mv;
+  // Q: (d, head, row) with element strides (1, q_sh, q_sb)
+  const cuuint64_t qd[3] = {(cuuint64_t)kD, (cuuint64_t)p.n_q_heads, (cuuint64_t)p.batch};
+  const cuuint64_t qs[2] = {(cuuint64_t)p.q_sh * 2,
+                            (cuuint64_t)(p.batch > 1 ? p.q_sb : p.q_sh * p.n_q_heads) * 2};
+  const cuuint32_t qbox[3] = {64, (cuuint32_t)q_rows, 1};
+  // K/V: (d, token, kv head, sequence) with element strides (1, D, kv_sh, kv_sb),
+  // or for a paged cache (d, row in page, kv head, page) over the page pool
+  const long long ps = paged ? (1ll << p.page_log2) : 0;
+  const int page_box = paged ? (int)(ps < kTile ? ps : kTile) : 0;
+  const cuuint64_t kd[4] = {(cuuint64_t)kD, (cuuint64_t)(paged ? ps : p.max_seq_len), (cuuint64_t)p.n_kv_heads,
+                            (cuuint64_t)(paged ? p.num_pages : nseq_kv)};
+  const cuuint64_t ks[3] = {
+      (cuuint64_t)kD * 2, (cuuint64_t)(paged ? ps * kD : p.kv_sh) * 2,
+      (cuuint64_t)(paged ? ps * kD * p.n_kv_heads : (nseq_kv > 1 ? p.kv_sb : p.kv_sh * p.n_kv_heads)) * 2};
+  const cuuint32_t kbox[4] = {64, (cuuint32_t)(paged ? page_box : kTile), 1, 1};
+  if (!make_tensor_map_bf16(&mq, p.q, 3, qd, qs, qbox) || !make_tensor_map_bf16(&mk, p.k, 4, kd, ks, kbox) ||
+      !make_tensor_map_bf16(&mv, p.v, 4, kd, ks, kbox))
+    return cudaErrorNotSupported;
+  {
+    // the shared-memory opt-in is per (kernel, device): set it once
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done.count({fn, dev})) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc);
+      if (e != cudaSuccess) return e;
+      done.insert({fn, dev});
+    }
+  }
+  TcDecodeArgs a{};
+  a.n_items = (unsigned)n_items;
+  a.kv_shared = kv_shared ? 1 : 0;
+  a.q_rows = q_rows;
+  a.page_box = page_box;
+  const int sms = device_sm_count();
+  const unsigned grid = (unsigned)(n_items < sms ? n_items : sms);
+  void* args[] = {&mq, &mk, &mv, const_cast<DecodeParams*>(&p), &a};
+  return cudaLaunchKernel(fn, dim3(grid), dim3(kThreads), args, kSmemAlloc, stream);
+}
+
+}  // namespace lara

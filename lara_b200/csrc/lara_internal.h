@@ -82,6 +82,10 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
 // geometry, or 0 when no kernel is compiled for it.
 int decode_tile_tokens(int head_dim, int group);
 
+// Granule of a caller-chosen chunk: the CUDA-core tile, or 128 tokens for a
+// geometry only the tensor-core kernel runs (group 16); 0 = unsupported.
+int decode_chunk_granule(int head_dim, int group);
+
 // Tokens of the first split for a (nsplit, chunk) plan, or 0 for equal
 // splits.  With two splits the first covers 7/8 of the span: all first
 // chunks launch before any second chunk, so the short second chunks fill the
@@ -90,6 +94,18 @@ int decode_tile_tokens(int head_dim, int group);
 int decode_first_chunk(int nsplit, int chunk, int group, int head_dim);
 
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream);
+
+// Tensor-core decode (decode_tc.cu): whether a (head_dim, group) geometry runs
+// on it (LARA_DECODE_PATH=simt|tc overrides the default, groups >= 8), its
+// split plan (any chunk works; the plan uses multiples of its 128-token tile),
+// and its launch.  The launch returns cudaErrorNotSupported when the tensors
+// cannot be described by tensor maps (alignment, paged cache); the caller then
+// runs the CUDA-core kernel.  The kernel keeps a work ticket and a finished-CTA
+// count in words 32 and 33 of the workspace's status block (zero between
+// launches; the last CTA resets them).
+bool decode_tc_selected(int head_dim, int group);
+void decode_tc_plan(int batch, int n_kv_heads, int max_tokens, const int32_t* lens_host, int* nsplit, int* chunk);
+cudaError_t decode_tc_launch(const DecodeParams& p, cudaStream_t stream);
 
 // Failure-detection self test: a bounded wait on a phase nothing completes;
 // sets kDevWaitTimeout in *status after limit_us.

@@ -55,7 +55,7 @@ extern "C" int lara_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_cach
   if (batch < 1 || n_q_heads < 1 || n_kv_heads < 1 || head_dim < 1 || max_seq_len < 1 ||
       n_q_heads % n_kv_heads != 0)
     return lara::set_last_error(LARA_ERR_BAD_CFG, "bad decode geometry");
-  const int tile = lara::decode_tile_tokens(head_dim, n_q_heads / n_kv_heads);
+  const int tile = lara::decode_chunk_granule(head_dim, n_q_heads / n_kv_heads);
   if (tile == 0) return lara::set_last_error(LARA_ERR_UNSUPPORTED, "no kernel compiled for this head geometry");
 
   int dev = 0;

@@ -22,11 +22,13 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_byte_addr, uint32_t
 }
 
 // kind::f16 instruction descriptor: bf16 x bf16 -> f32 accumulate, M x N tile,
-// A K-major, B K-major (b_mn_major = 0) or MN-major (1).
-__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t m, uint32_t n, uint32_t b_mn_major) {
+// B K-major (b_mn_major = 0) or MN-major (1), A likewise (a_mn_major).
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t m, uint32_t n, uint32_t b_mn_major,
+                                                  uint32_t a_mn_major = 0) {
   return (1u << 4)              // D format f32
          | (1u << 7)            // A format bf16
          | (1u << 10)           // B format bf16
+         | (a_mn_major << 15)   // A major (0 = K, 1 = MN)
          | (b_mn_major << 16)   // B major (0 = K, 1 = MN)
          | ((n >> 3) << 17)
          | ((m >> 4) << 24);
@@ -88,6 +90,27 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
+// 8 / 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // 16 consecutive 32-bit columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
   asm volatile(
@@ -116,6 +139,22 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       "[%2];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
+}
+
+// 4-D tensor-map load with an L2 cache policy (e.g. evict-first for data read once).
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                                 uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
+      : "memory");
+}
+
+// Orders this thread's generic shared-memory writes before later async-proxy
+// reads (tcgen05.mma operands, bulk copies).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Bounded wait that also gives up once another role has aborted.

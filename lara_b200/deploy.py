@@ -55,10 +55,11 @@ SCHEMA_DEPLOY = "lara-b200-deployment-v1"
 SCHEMA_ENV = "lara-b200-environment-v1"
 DEFAULT_NAME = "lara_attention"  # sw/run_board_full_validation.py default --bitstream ./lara_attention.bit
 
-# Kernel geometries compiled into the library (lara_b200/csrc/decode.cu and
-# prefill_tc.cu instantiate exactly these).
+# Kernel geometries compiled into the library (lara_b200/csrc/decode.cu,
+# decode_tc.cu and prefill_tc.cu instantiate exactly these).
 DECODE_HEAD_DIMS = (64, 128)
 DECODE_GROUP_SIZES = (1, 2, 4, 8)
+TENSOR_CORE_DECODE_GROUP_SIZES = (1, 2, 4, 8, 16)
 TENSOR_CORE_HEAD_DIMS = (128,)
 
 
@@ -104,7 +105,8 @@ def write_descriptors(out_dir: str | Path, name: str = DEFAULT_NAME, arithmetic:
               "abi_version": int(nat.lib.lara_abi_version()), "arithmetic": arithmetic},
         hwh: {**common, "kind": "hardware_handoff",
               "decode_kernel": {"head_dims": list(DECODE_HEAD_DIMS), "group_sizes": list(DECODE_GROUP_SIZES)},
-              "tensor_core_kernel": {"head_dims": list(TENSOR_CORE_HEAD_DIMS)},
+              "tensor_core_kernel": {"head_dims": list(TENSOR_CORE_HEAD_DIMS),
+                                     "decode_group_sizes": list(TENSOR_CORE_DECODE_GROUP_SIZES)},
               "driver_defaults": {"n_q_heads": drv.N_Q_HEADS, "n_kv_heads": drv.N_KV_HEADS,
                                   "head_dim": drv.HEAD_DIM, "max_seq_len": drv.MAX_SEQ_LEN,
                                   "absolute_position_limit": drv.ABSOLUTE_POSITION_LIMIT,

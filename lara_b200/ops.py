@@ -120,6 +120,14 @@ class Decoder:
         return ml, acc
 
 
+def decode_kernel(n_q_heads: int, n_kv_heads: int, head_dim: int) -> str:
+    """``"tensor"`` (tcgen05 kernel) or ``"cuda_core"``: which decode kernel runs a geometry."""
+    from ._native import LARA_DECODE_KERNEL_TENSOR
+
+    k = int(lib.lara_decode_kernel(int(n_q_heads), int(n_kv_heads), int(head_dim)))
+    return "tensor" if k == LARA_DECODE_KERNEL_TENSOR else "cuda_core"
+
+
 def gqa_decode(q, k_cache, v_cache, seq_lens, *, scale=None, num_splits=0, chunk_tokens=0):
     """One-shot decode (plans and allocates a workspace per call)."""
     B, Hq, D = q.shape

@@ -86,19 +86,25 @@ def _fill(cache, torch, k, v, lens, dev, chunks=(None,)):
     return slots
 
 
-GEOMS = [(128, 4), (128, 8), (64, 4), (128, 1)]
+GEOMS = [(128, 4), (128, 8), (64, 4), (128, 1), (128, 16)]
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("path", ["auto", "tc", "simt"])
 @pytest.mark.parametrize("page_size", [16, 64, 256])
 @pytest.mark.parametrize("geom", GEOMS, ids=lambda g: f"D{g[0]}_G{g[1]}")
-def test_paged_decode_equals_contiguous(page_size, geom):
+def test_paged_decode_equals_contiguous(monkeypatch, page_size, geom, path):
+    """Both decode kernels (LARA_DECODE_PATH=tc|simt, and the default choice)."""
     torch = _torch()
     from lara_b200 import ops
     from lara_b200.paged import PagedKVCache
     from parity import assert_bf16_parity, words_of
 
     D, G = geom
+    if (path == "tc" and D != 128) or (path == "simt" and G > 8):
+        pytest.skip("geometry not compiled for this kernel")
+    if path != "auto":
+        monkeypatch.setenv("LARA_DECODE_PATH", path)
     hkv = 2
     hq = hkv * G
     lens = [700, 1, 0, 513, 64]
