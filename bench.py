@@ -52,7 +52,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "GQA decode KV-stream GB/s (% of HBM peak) & queries/s at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
-PROFILE_SUMMARY = ROOT / "profiles" / "decode_llama3_8b_cfg2.txt"
+# ncu summaries per workload (dram traffic per launch of the full workload)
+PROFILE_SUMMARIES = {"llama3_8b_decode": ROOT / "profiles" / "decode_llama3_8b_cfg2.txt",
+                     "ragged_decode_stress": ROOT / "profiles" / "decode_tc_ragged_cfg3.txt"}
 
 
 def parse_args():
@@ -64,7 +66,9 @@ def parse_args():
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5, 6], default=2,
                     help="BASELINE config (2 = the headline Llama-3-8B decode; 5 = chunked prefill); "
                          "6 = the layer prologue (RMSNorm + QKV projection + RoPE) of config 5's new tokens")
-    ap.add_argument("--batch", type=int, default=None, help="sequences per rank (default: config 2's 64)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="config 2/4: sequences per rank (default 64 / 8); config 3: the first N of its 256 "
+                         "ragged sequences (a smaller case for profiling)")
     ap.add_argument("--seq-len", type=int, default=None)
     ap.add_argument("--splits", type=int, default=0, help="force the split count (0 = planner)")
     ap.add_argument("--chunk", type=int, default=0)
@@ -94,11 +98,12 @@ def measured_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic():
-    """dram bytes per launch from the committed ncu summary, if present."""
-    if not PROFILE_SUMMARY.exists():
+def profiled_traffic(workload: str):
+    """dram bytes per launch from the workload's committed ncu summary, if present."""
+    path = PROFILE_SUMMARIES.get(workload)
+    if path is None or not path.exists():
         return None
-    for line in PROFILE_SUMMARY.read_text().splitlines():
+    for line in path.read_text().splitlines():
         if line.startswith("traffic_bytes_per_launch:"):
             try:
                 return int(float(line.split(":", 1)[1].strip()))
@@ -327,12 +332,12 @@ def _setup_decode(args, cfg, rank, world, dev):
         q, k, v, lens = make_decode_inputs(cfg, dev, batch=B, seq_len=L, seed=cfg.seed + 1000 * rank)
         scaling, global_batch = "weak", B * world
     elif cfg.name == "ragged_decode_stress":
-        all_lens = cfg.lens()
-        mine = parallel.balanced_partition(all_lens, world)[rank] if world > 1 else list(range(cfg.batch))
+        all_lens = cfg.lens(args.batch)  # --batch N: the first N sequences (small profiling case)
+        mine = parallel.balanced_partition(all_lens, world)[rank] if world > 1 else list(range(len(all_lens)))
         L = int(all_lens[mine].max())
         q, k, v, lens = make_decode_inputs(cfg, dev, lens=all_lens[mine], capacity=L, seed=cfg.seed + 1000 * rank)
         B = len(mine)
-        scaling, global_batch = "strong", cfg.batch
+        scaling, global_batch = "strong", len(all_lens)
         info["sequences_on_rank0"] = len(mine)
     else:  # long-context split-KV
         B = args.batch or cfg.batch
@@ -527,7 +532,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     peak, peak_kind = measured_peak()
     value = total_bytes / (ms * 1e-3) / 1e9
     achieved = nbytes / (ms * 1e-3) / 1e9  # this GPU's bytes over the step
-    traffic = profiled_traffic() if cfg.name == "llama3_8b_decode" and not args.paged else None
+    full_size = args.batch is None and args.seq_len is None
+    traffic = profiled_traffic(cfg.name) if full_size and not args.paged else None
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()

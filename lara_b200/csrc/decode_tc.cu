@@ -43,12 +43,15 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <set>
 #include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "decode_merge.cuh"
@@ -140,6 +143,61 @@ __device__ __forceinline__ int row_len(const DecodeParams& p, int seq, int row_i
     len += l;
   }
   return len < 0 ? 0 : (len > p.max_seq_len ? p.max_seq_len : (int)len);
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(kFull, x, off);
+  return x;
+}
+
+// Merge the split partials of (row b, kv head kvh) with the log-sum-exp rule
+// (M = max m_s, L = sum l_s 2^(m_s - M), o = sum acc_s 2^(m_s - M) / L).
+// Warp w takes heads w, w + 4, ...; lane i holds split i's weight and dims
+// 4i .. 4i+3 of the accumulator, so every load of a pass is independent.
+template <int G>
+__device__ __forceinline__ void merge_splits_tc(const DecodeParams& p, int b, int kvh, int nsplit_b,
+                                                bool partial_out, int warp, int lane) {
+  for (int g = warp; g < G; g += 4) {
+    const int h = kvh * G + g;
+    const long long row = (long long)b * p.n_q_heads + h;
+    const float* ml = p.part_ml + row * p.nsplit * 2;
+    const float* pa = p.part_acc + row * p.nsplit * kD;
+    float M = -INFINITY;
+    for (int s = lane; s < nsplit_b; s += 32) M = fmaxf(M, __ldcg(ml + 2 * s));
+    M = warp_max(M);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < nsplit_b; s0 += 32) {
+      const int sl = s0 + lane;
+      const float2 mls = sl < nsplit_b ? __ldcg(reinterpret_cast<const float2*>(ml + 2 * sl)) : make_float2(0.f, 0.f);
+      const float w_lane = sl < nsplit_b ? exp2f(mls.x - Mu) : 0.f;
+      L = fmaf(mls.y, w_lane, L);
+      const int cnt = min(32, nsplit_b - s0);
+#pragma unroll 8
+      for (int j = 0; j < cnt; ++j) {
+        const float w = __shfl_sync(kFull, w_lane, j);
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(pa + (long long)(s0 + j) * kD) + lane);
+        o.x = fmaf(a.x, w, o.x);
+        o.y = fmaf(a.y, w, o.y);
+        o.z = fmaf(a.z, w, o.z);
+        o.w = fmaf(a.w, w, o.w);
+      }
+    }
+    L = warp_sum(L);
+    if (partial_out) {
+      float2* dst = reinterpret_cast<float2*>(p.out_acc + row * kD + 4 * lane);  // out_acc is 8-byte aligned
+      dst[0] = make_float2(o.x, o.y);
+      dst[1] = make_float2(o.z, o.w);
+      if (lane == 0) { p.out_ml[row * 2] = M; p.out_ml[row * 2 + 1] = L; }
+    } else {
+      const float inv = (L > 0.f) ? 1.f / L : 0.f;
+      uint32_t* dst = reinterpret_cast<uint32_t*>(p.o + b * p.o_sb + h * p.o_sh + 4 * lane);
+      dst[0] = pack2_bf16(o.x * inv, o.y * inv);
+      dst[1] = pack2_bf16(o.z * inv, o.w * inv);
+    }
+  }
 }
 
 // 128-thread meeting point of the softmax warps on an mbarrier (bounded).
@@ -262,20 +320,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       bool ok = true;
+      // The next ticket is taken while the current item streams, and a row's
+      // length is loaded once for its consecutive kv heads.
+      unsigned next = atomicAdd(queue, 1u);
+      int len_row = -1, len = 0;
       while (ok) {
-        const unsigned item = atomicAdd(queue, 1u);
+        const unsigned item = next;
         Meta m{};
         if (item >= a.n_items) {
           m.kind = kEntryEnd;
           (void)push(m, false);
           break;
         }
+        next = atomicAdd(queue, 1u);
         const int split = (int)(item / (unsigned)per_split);
         const int rem = (int)(item - (unsigned)split * (unsigned)per_split);
         const int b = rem / p.n_kv_heads;
         const int kvh = rem - b * p.n_kv_heads;
         const int seq = b / p.rows_per_seq;
-        const int len = row_len(p, seq, b - seq * p.rows_per_seq);
+        if (b != len_row) {
+          len = row_len(p, seq, b - seq * p.rows_per_seq);
+          len_row = b;
+        }
         const int tok_begin = split == 0 ? 0 : c0 + (split - 1) * p.chunk;
         m.row = b;
         m.kvh = kvh;
@@ -468,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!group_sync(&bars->sync, sync_phase, abort)) return false;
       if (*bcast) {
         __threadfence();
-        merge_split_partials<kD>(p, b, kvh, G, m.nsplit_b, partial_out, t, 128);
+        merge_splits_tc<G>(p, b, kvh, m.nsplit_b, partial_out, warp, lane);
       }
       return true;
     };
@@ -646,50 +712,51 @@ bool decode_tc_selected(int head_dim, int group) {
 
 void decode_tc_plan(int batch, int n_kv_heads, int max_tokens, const int32_t* lens_host, int* nsplit_out,
                     int* chunk_out) {
-  // Items are dispensed one by one to resident CTAs (one per SM), so the step
-  // takes about (total tiles + per-item overhead) / SMs plus the last item.
-  constexpr double kItemOverhead = 0.35;  // tiles of stream time an item costs beyond its own tiles
-  const double sms = device_sm_count();
+  // Items are dispensed in ticket order (split-major) to whichever CTA (one
+  // per SM) is free, so the plan simulates that list schedule for each
+  // candidate chunk and keeps the one whose last CTA finishes first.  An
+  // item costs its tiles plus about one tile of stream time at its boundary
+  // (B200 sweeps of configs 2 and 3: 1-3 us per item, one tile ~1.6 us).
+  constexpr double kItemOverhead = 1.0;
+  constexpr long long kMaxItems = 1 << 18;  // candidates with more items are not simulated
+  const int sms = device_sm_count() > 0 ? device_sm_count() : 148;
   const int L = max_tokens < 1 ? 1 : max_tokens;
   const int max_tiles = (L + kTile - 1) / kTile;
+  std::vector<int> len(batch);
+  for (int b = 0; b < batch; ++b)
+    len[b] = lens_host ? (lens_host[b] < 0 ? 0 : (lens_host[b] > L ? L : lens_host[b])) : L;
   double best = 1e300;
   int best_chunk = max_tiles * kTile, best_s = 1;
+  std::vector<double> heap;
   for (long long chunk = kTile;; chunk *= 2) {
     if (chunk > (long long)max_tiles * kTile) chunk = (long long)max_tiles * kTile;
     const int c = (int)chunk;
-    double tiles = 0.0, items = 0.0;
-    long long longest = 0;
-    for (int b = 0; b < (lens_host ? batch : 1); ++b) {
-      const int len = lens_host ? (lens_host[b] < 0 ? 0 : (lens_host[b] > L ? L : lens_host[b])) : L;
-      if (len == 0) {
-        items += 1;
-        continue;
+    const int ns = (L + c - 1) / c;
+    if ((long long)ns * batch * n_kv_heads <= kMaxItems) {
+      heap.assign((size_t)sms, 0.0);  // min-heap of CTA finish times
+      auto take = [&](double cost) {
+        std::pop_heap(heap.begin(), heap.end(), std::greater<double>());
+        heap.back() += cost;
+        std::push_heap(heap.begin(), heap.end(), std::greater<double>());
+      };
+      for (int sp = 0; sp < ns; ++sp)
+        for (int b = 0; b < batch; ++b) {
+          const long long begin = (long long)sp * c;
+          if (len[b] == 0 && sp == 0) {
+            for (int h = 0; h < n_kv_heads; ++h) take(kItemOverhead);
+            continue;
+          }
+          if (begin >= len[b]) continue;
+          const long long ntok = std::min<long long>(c, len[b] - begin);
+          const double cost = (double)((ntok + kTile - 1) / kTile) + kItemOverhead;
+          for (int h = 0; h < n_kv_heads; ++h) take(cost);
+        }
+      const double makespan = *std::max_element(heap.begin(), heap.end());
+      if (makespan < best * (1.0 - 1e-9)) {
+        best = makespan;
+        best_chunk = c;
+        best_s = ns;
       }
-      const int ns = (len + c - 1) / c;
-      const int last = len - (ns - 1) * c;
-      tiles += (double)(ns - 1) * (c / kTile) + (double)((last + kTile - 1) / kTile);
-      items += ns;
-      const long long first = len < c ? len : c;
-      if (first > longest) longest = first;
-    }
-    if (!lens_host) {
-      tiles *= batch;
-      items *= batch;
-    }
-    tiles *= n_kv_heads;
-    items *= n_kv_heads;
-    const double per_item = (double)((longest + kTile - 1) / kTile) + kItemOverhead;
-    double cost;
-    if (!lens_host) {
-      // equal items: whole waves of them
-      cost = std::ceil(items / sms) * per_item;
-    } else {
-      cost = (tiles + items * kItemOverhead) / sms + per_item;
-    }
-    if (cost < best * (1.0 - 1e-9)) {
-      best = cost;
-      best_chunk = c;
-      best_s = (L + c - 1) / c;
     }
     if (c >= max_tiles * kTile) break;
   }
