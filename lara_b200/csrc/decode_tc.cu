@@ -78,7 +78,9 @@ constexpr int kPOff = kQOff + 2 * kOpBytes;         // two tile buffers x (P_hi,
 constexpr int kXOff = kPOff + 4 * kOpBytes;         // exchange: tile max [2][4][16], row sums [4][16], flag
 constexpr int kMetaOff = kXOff + 1024;
 constexpr int kBarOff = kMetaOff + 256;
-constexpr int kSmemAlloc = kBarOff + 256 + 1024;    // + slack for 1024-byte alignment
+constexpr int kPageCache = 512;                     // block-table entries of an item kept in shared memory
+constexpr int kPageOff = kBarOff + 256;
+constexpr int kSmemAlloc = kPageOff + kPageCache * 4 + 1024;  // + slack for 1024-byte alignment
 constexpr uint32_t kTmemCols = 64;
 constexpr int kTmaWarp = 4;
 constexpr int kMmaWarp = 5;
@@ -261,121 +263,140 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kTmaWarp) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const uint64_t pol = make_evict_first_policy();
-      const int per_split = p.batch * p.n_kv_heads;
-      const int c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
-      const uint32_t q_bytes = 2u * 128u * (uint32_t)a.q_rows;
-      int n = 0, qi = 0;
-      auto push = [&](const Meta& m, bool copies) -> bool {
-        const int st = n % kStages;
-        if (n >= kStages && !wait_or_abort(&bars->empty[st], ((n / kStages) - 1) & 1, abort)) return false;
-        metas[st] = m;
-        if (copies && a.page_box == 0) {
-          uint8_t* ks = smem + kKOff + st * kKVBytes;
-          uint8_t* vs = smem + kVOff + st * kKVBytes;
-          mbar_arrive_expect_tx(&bars->full[st], 2 * kKVBytes);
-          tma_load_4d_hint(ks, &tm_k, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
-          tma_load_4d_hint(ks + kHalf, &tm_k, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
-          tma_load_4d_hint(vs, &tm_v, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
-          tma_load_4d_hint(vs + kHalf, &tm_v, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
-        } else if (copies) {
-          // paged cache: the tile is page_box-row pieces of whole pages (tiles
-          // start on 128-token boundaries); pieces past the item's end are not
-          // loaded (their rows are masked, and V rows zeroed, by the softmax)
-          uint8_t* ks = smem + kKOff + st * kKVBytes;
-          uint8_t* vs = smem + kVOff + st * kKVBytes;
-          const int bx = a.page_box;
-          const int pieces = min(kTile / bx, (m.tok_end - m.tok0 + bx - 1) / bx);
-          int pages[kTile / 16];
-          const int32_t* row = p.block_table + (long long)m.seq_kv * p.pages_per_seq;
-#pragma unroll
-          for (int i = 0; i < kTile / 16; ++i) {
-            if (i < pieces) {
-              int pg = __ldg(row + ((m.tok0 + i * bx) >> p.page_log2));
-              if (pg < 0 || pg >= p.num_pages) {
-                atomicOr(p.status, kDevBadPage);
-                pg = 0;  // keep every copy in bounds
-              }
-              pages[i] = pg;
-            }
-          }
-          mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
-          const int ps_mask = (1 << p.page_log2) - 1;
-#pragma unroll
-          for (int i = 0; i < kTile / 16; ++i) {
-            if (i < pieces) {
-              const int in_page = (m.tok0 + i * bx) & ps_mask;
-              const int off = i * bx * 128;
-              tma_load_4d_hint(ks + off, &tm_k, 0, in_page, m.kvh, pages[i], &bars->full[st], pol);
-              tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, in_page, m.kvh, pages[i], &bars->full[st], pol);
-              tma_load_4d_hint(vs + off, &tm_v, 0, in_page, m.kvh, pages[i], &bars->full[st], pol);
-              tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, in_page, m.kvh, pages[i], &bars->full[st], pol);
-            }
-          }
-        } else {
-          mbar_arrive(&bars->full[st]);
+    // Lane 0 issues every copy.  For a paged cache the whole warp first loads
+    // the item's block-table entries into a shared-memory cache, so a tile
+    // costs no dependent global load (one load latency per item).
+    const uint64_t pol = make_evict_first_policy();
+    const int per_split = p.batch * p.n_kv_heads;
+    const int c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
+    const uint32_t q_bytes = 2u * 128u * (uint32_t)a.q_rows;
+    int* pcache = reinterpret_cast<int*>(smem + kPageOff);
+    const int32_t* bt_row = p.block_table;
+    int pg0 = 0;  // page index held by cache entry 0 (current item)
+    int n = 0, qi = 0;
+    auto page_at = [&](int tok) -> int {
+      const int idx = (tok >> p.page_log2) - pg0;
+      int pg = idx < kPageCache ? pcache[idx] : __ldg(bt_row + (tok >> p.page_log2));
+      if (pg < 0 || pg >= p.num_pages) {
+        atomicOr(p.status, kDevBadPage);
+        pg = 0;  // keep every copy in bounds
+      }
+      return pg;
+    };
+    auto push = [&](const Meta& m, bool copies) -> bool {  // lane 0
+      const int st = n % kStages;
+      if (n >= kStages && !wait_or_abort(&bars->empty[st], ((n / kStages) - 1) & 1, abort)) return false;
+      metas[st] = m;
+      if (copies && a.page_box == 0) {
+        uint8_t* ks = smem + kKOff + st * kKVBytes;
+        uint8_t* vs = smem + kVOff + st * kKVBytes;
+        mbar_arrive_expect_tx(&bars->full[st], 2 * kKVBytes);
+        tma_load_4d_hint(ks, &tm_k, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+        tma_load_4d_hint(ks + kHalf, &tm_k, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+        tma_load_4d_hint(vs, &tm_v, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+        tma_load_4d_hint(vs + kHalf, &tm_v, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+      } else if (copies) {
+        // paged cache: the tile is page_box-row pieces of whole pages (tiles
+        // start on 128-token boundaries); pieces past the item's end are not
+        // loaded (their rows are masked, and V rows zeroed, by the softmax)
+        uint8_t* ks = smem + kKOff + st * kKVBytes;
+        uint8_t* vs = smem + kVOff + st * kKVBytes;
+        const int bx = a.page_box;
+        const int pieces = min(kTile / bx, (m.tok_end - m.tok0 + bx - 1) / bx);
+        mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
+        const int ps_mask = (1 << p.page_log2) - 1;
+        for (int i = 0; i < pieces; ++i) {
+          const int tok = m.tok0 + i * bx;
+          const int pg = page_at(tok);
+          const int in_page = tok & ps_mask;
+          const int off = i * bx * 128;
+          tma_load_4d_hint(ks + off, &tm_k, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+          tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+          tma_load_4d_hint(vs + off, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+          tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
         }
-        bars->issued = ++n;
-        return true;
-      };
-      bool ok = true;
-      // The next ticket is taken while the current item streams, and a row's
-      // length is loaded once for its consecutive kv heads.
-      unsigned next = atomicAdd(queue, 1u);
-      int len_row = -1, len = 0;
-      while (ok) {
-        const unsigned item = next;
-        Meta m{};
-        if (item >= a.n_items) {
+      } else {
+        mbar_arrive(&bars->full[st]);
+      }
+      bars->issued = ++n;
+      return true;
+    };
+    bool ok = true;
+    // The next ticket is taken while the current item streams, and a row's
+    // length is loaded once for its consecutive kv heads.
+    unsigned next = 0;
+    if (lane == 0) next = atomicAdd(queue, 1u);
+    int len_row = -1, len = 0;
+    while (true) {
+      const unsigned item = __shfl_sync(kFull, next, 0);
+      Meta m{};
+      if (item >= a.n_items) {
+        if (lane == 0) {
           m.kind = kEntryEnd;
           (void)push(m, false);
-          break;
         }
-        next = atomicAdd(queue, 1u);
-        const int split = (int)(item / (unsigned)per_split);
-        const int rem = (int)(item - (unsigned)split * (unsigned)per_split);
-        const int b = rem / p.n_kv_heads;
-        const int kvh = rem - b * p.n_kv_heads;
-        const int seq = b / p.rows_per_seq;
-        if (b != len_row) {
-          len = row_len(p, seq, b - seq * p.rows_per_seq);
-          len_row = b;
-        }
-        const int tok_begin = split == 0 ? 0 : c0 + (split - 1) * p.chunk;
-        m.row = b;
-        m.kvh = kvh;
-        m.split = split;
-        if (len == 0) {
-          // no visible key: split 0 writes the zero output (the RTL normaliser maps l == 0 to 0)
-          if (split != 0) continue;
-          m.kind = kEntryZero;
-          ok = push(m, false);
-          continue;
-        }
-        if (tok_begin >= len) continue;
-        const int ntok = min(len - tok_begin, split == 0 ? c0 : p.chunk);
-        m.kind = kEntryTile;
-        m.tok_end = tok_begin + ntok;
-        m.nsplit_b = len <= c0 ? 1 : 1 + (len - c0 + p.chunk - 1) / p.chunk;
-        m.seq_kv = a.kv_shared ? 0 : seq;
+        break;
+      }
+      if (lane == 0) next = atomicAdd(queue, 1u);
+      const int split = (int)(item / (unsigned)per_split);
+      const int rem = (int)(item - (unsigned)split * (unsigned)per_split);
+      const int b = rem / p.n_kv_heads;
+      const int kvh = rem - b * p.n_kv_heads;
+      const int seq = b / p.rows_per_seq;
+      if (b != len_row) {
+        int l = 0;
+        if (lane == 0) l = row_len(p, seq, b - seq * p.rows_per_seq);
+        len = __shfl_sync(kFull, l, 0);
+        len_row = b;
+      }
+      const int tok_begin = split == 0 ? 0 : c0 + (split - 1) * p.chunk;
+      m.row = b;
+      m.kvh = kvh;
+      m.split = split;
+      if (len == 0) {
+        // no visible key: split 0 writes the zero output (the RTL normaliser maps l == 0 to 0)
+        if (split != 0) continue;
+        m.kind = kEntryZero;
+        if (lane == 0) ok = push(m, false);
+        if (!__shfl_sync(kFull, ok, 0)) break;
+        continue;
+      }
+      if (tok_begin >= len) continue;
+      const int ntok = min(len - tok_begin, split == 0 ? c0 : p.chunk);
+      m.kind = kEntryTile;
+      m.tok_end = tok_begin + ntok;
+      m.nsplit_b = len <= c0 ? 1 : 1 + (len - c0 + p.chunk - 1) / p.chunk;
+      m.seq_kv = a.kv_shared ? 0 : seq;
+      if (a.page_box) {
+        bt_row = p.block_table + (long long)seq * p.pages_per_seq;
+        pg0 = tok_begin >> p.page_log2;
+        const int np = min(kPageCache, ((m.tok_end - 1) >> p.page_log2) - pg0 + 1);
+        for (int i = lane; i < np; i += 32) pcache[i] = __ldg(bt_row + pg0 + i);
+        __syncwarp();
+      }
+      if (lane == 0) {
         // the item's query heads (rows past the group are never used)
         const int qs = qi & 1;
-        if (qi >= 2 && !wait_or_abort(&bars->q_free[qs], ((qi - 2) >> 1) & 1, abort)) break;
-        uint8_t* qd = smem + kQOff + qs * kOpBytes;
-        mbar_arrive_expect_tx(&bars->q_full[qs], q_bytes);
-        tma_load_3d(qd, &tm_q, 0, kvh * G, b, &bars->q_full[qs]);
-        tma_load_3d(qd + kOpBytes / 2, &tm_q, 64, kvh * G, b, &bars->q_full[qs]);
-        m.qslot = qs;
-        m.qpar = (qi >> 1) & 1;
-        bars->q_issued = ++qi;
-        const int ntiles = (ntok + kTile - 1) / kTile;
-        for (int j = 0; ok && j < ntiles; ++j) {
-          m.tok0 = tok_begin + j * kTile;
-          m.flags = (j == 0 ? 1 : 0) | (j == ntiles - 1 ? 2 : 0);
-          ok = push(m, true);
+        if (qi >= 2 && !wait_or_abort(&bars->q_free[qs], ((qi - 2) >> 1) & 1, abort)) {
+          ok = false;
+        } else {
+          uint8_t* qd = smem + kQOff + qs * kOpBytes;
+          mbar_arrive_expect_tx(&bars->q_full[qs], q_bytes);
+          tma_load_3d(qd, &tm_q, 0, kvh * G, b, &bars->q_full[qs]);
+          tma_load_3d(qd + kOpBytes / 2, &tm_q, 64, kvh * G, b, &bars->q_full[qs]);
+          m.qslot = qs;
+          m.qpar = (qi >> 1) & 1;
+          bars->q_issued = ++qi;
+          const int ntiles = (ntok + kTile - 1) / kTile;
+          for (int j = 0; ok && j < ntiles; ++j) {
+            m.tok0 = tok_begin + j * kTile;
+            m.flags = (j == 0 ? 1 : 0) | (j == ntiles - 1 ? 2 : 0);
+            ok = push(m, true);
+          }
         }
       }
+      // lane 0 is done with this item's cache entries
+      if (!__shfl_sync(kFull, ok, 0)) break;
     }
   } else if (warp == kMmaWarp) {
     // ----------------------------------------------------------------- MMA
