@@ -687,7 +687,8 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
         "config": {"workload": cfg.name, "batch_per_gpu": B, "new_tokens": n, "cached_tokens": C,
                    "n_q_heads": cfg.n_q_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
                    "causal": True, "step": "length reset + K/V append + attention",
-                   "split_p": os.environ.get("LARA_TC_SPLIT_P", "1") != "0"},
+                   "p_precision": "bf16 RNE (LARA_TC_SPLIT_P=0)" if os.environ.get("LARA_TC_SPLIT_P") == "0"
+                   else "P_hi + P_lo"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_flop_per_launch": flops, "attention_kernel_ms": round(k_ms, 4)},

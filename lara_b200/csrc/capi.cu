@@ -154,8 +154,10 @@ AttnPath attn_path_override() {
 // -1 when the streaming kernel should run instead, or an error code.
 int try_tensor_path(lara::PrefillTcParams tp, cudaStream_t st) {
   const AttnPath path = attn_path_override();
-  // LARA_TC_SPLIT_P=0 rounds P to one bf16 (faster, ~1 bf16 ulp of the row
-  // scale); the default splits P into two bf16 terms.
+  // By default P is split into two bf16 terms (P_hi + P_lo, ~16 significant
+  // bits, two P.V passes) so the output meets the <= 2 ulp parity bound;
+  // LARA_TC_SPLIT_P=0 rounds P to one bf16 (RNE, the FlashAttention choice:
+  // faster, error ~1 bf16 ulp of the head vector's largest element).
   const char* sp = std::getenv("LARA_TC_SPLIT_P");
   tp.split_p = (sp && std::strcmp(sp, "0") == 0) ? 0 : 1;
   if (path == AttnPath::kStream) return -1;

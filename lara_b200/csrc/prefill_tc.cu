@@ -104,7 +104,7 @@ struct PPBars {
 };
 static_assert(sizeof(PPBars) <= 256, "barrier block");
 
-template <bool kSplitP>
+template <bool kSplitP, bool kPairRows>
 __global__ void __launch_bounds__(kPPThreads, 1)
     prefill_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], 8 * 32);
+      mbar_init(&bars->p_full[t], kPairRows ? 8 * 32 : kTileM);
       mbar_init(&bars->o_full[t], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -250,77 +250,213 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    // All 8 warps take tile A then tile B: two threads per query row (warps
-    // w and w + 4 share a TMEM lane quarter), each owning 64 of the 128
-    // columns; the pair exchanges row maxima (and, at the end, row sums)
-    // through shared memory under a 64-thread named barrier.
-    const int quarter = warp & 3;
-    const int ch = warp >> 2;            // column half
-    const int r = quarter * 32 + lane;   // row within a tile
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int pair_bar = 1 + quarter;
-    float* red = reinterpret_cast<float*>(smem + kPPRedOff);  // [parity][half][row]
-    float m_ref[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.f, 0.f};
-    long long vis_row[2], vis_min[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const int q_row = q0 + t * kTileM + r;
-      vis_row[t] = a.causal ? min((long long)kv_len, (long long)q_off + q_row + 1) : (long long)kv_len;
-      vis_min[t] = a.causal ? min((long long)kv_len, (long long)q_off + q0 + t * kTileM + 1) : (long long)kv_len;
-    }
-    bool ok = true;
-    int step = 0;  // parity of the exchange buffer
-    for (int j = 0; ok && j < ntiles; ++j) {
-#pragma unroll
-      for (int t = 0; t < 2; ++t, ++step) {
-        const uint32_t s_tm = tmem + lane_off + t * 128;
+    if constexpr (kPairRows) {
+      // All 8 warps take tile A then tile B: two threads per query row (warps
+      // w and w + 4 share a TMEM lane quarter), each owning 64 of the 128
+      // columns; the pair exchanges row maxima (and, at the end, row sums)
+      // through shared memory under a 64-thread named barrier.
+      const int quarter = warp & 3;
+      const int ch = warp >> 2;            // column half
+      const int r = quarter * 32 + lane;   // row within a tile
+      const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+      const int pair_bar = 1 + quarter;
+      float* red = reinterpret_cast<float*>(smem + kPPRedOff);  // [parity][half][row]
+      float m_ref[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.f, 0.f};
+      long long vis_row[2], vis_min[2];
+  #pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int q_row = q0 + t * kTileM + r;
+        vis_row[t] = a.causal ? min((long long)kv_len, (long long)q_off + q_row + 1) : (long long)kv_len;
+        vis_min[t] = a.causal ? min((long long)kv_len, (long long)q_off + q0 + t * kTileM + 1) : (long long)kv_len;
+      }
+      bool ok = true;
+      int step = 0;  // parity of the exchange buffer
+      for (int j = 0; ok && j < ntiles; ++j) {
+  #pragma unroll
+        for (int t = 0; t < 2; ++t, ++step) {
+          const uint32_t s_tm = tmem + lane_off + t * 128;
+          const uint32_t o_tm = tmem + lane_off + 256 + t * 128 + ch * 64;
+          if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[t], j & 1, abort))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          float sv[64];
+          tmem_ld32(s_tm + ch * 64, sv);
+          tmem_ld32(s_tm + ch * 64 + 32, sv + 32);
+          tmem_wait_ld();
+          if ((long long)(j + 1) * kTileN > vis_min[t]) {
+            const long long vis = vis_row[t] - (long long)j * kTileN - ch * 64;  // visible columns of this half
+  #pragma unroll
+            for (int c = 0; c < 64; ++c)
+              if (c >= vis) sv[c] = -INFINITY;
+          }
+          // three-input max.f32 (sm_100): two new scores per instruction, 4 chains
+          float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+  #pragma unroll
+          for (int c = 4; c < 64; c += 2)
+            asm("max.f32 %0, %0, %1, %2;" : "+f"(mx4[(c >> 1) & 3]) : "f"(sv[c]), "f"(sv[c + 1]));
+          float* rbuf = red + (step & 1) * 2 * kTileM;
+          rbuf[ch * kTileM + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+          asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+          const float mx = fmaxf(rbuf[r], rbuf[kTileM + r]);
+          const float m_tile = mx * a.scale_log2;  // scale > 0 keeps the order
+          const bool move = m_tile > m_ref[t] + kRescaleThreshold || (m_ref[t] == -INFINITY && m_tile != -INFINITY);
+          const float m_new = move ? m_tile : m_ref[t];
+          const float corr = move ? exp2f(m_ref[t] - m_new) : 1.f;
+          const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+          // packed fp32 pairs: scale-and-shift, sum and the split residual each
+          // take one FFMA2 / FADD2 per two scores; exp2 is the MUFU instruction
+          // (ex2.approx, relative error ~2^-22, far below the 2^-16 of split P)
+          float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+          const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
+          const float2 nm2 = make_float2(-m_use, -m_use);
+  #pragma unroll
+          for (int c = 0; c < 64; c += 32) {
+            uint32_t pw[16];
+            uint32_t lw[kSplitP ? 16 : 1];
+  #pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const float2 x = __ffma2_rn(make_float2(sv[c + i], sv[c + i + 1]), sc2, nm2);
+              float2 pp;
+              asm("ex2.approx.f32 %0, %1;" : "=f"(pp.x) : "f"(x.x));
+              asm("ex2.approx.f32 %0, %1;" : "=f"(pp.y) : "f"(x.y));
+              sum2[(i >> 1) & 1] = __fadd2_rn(sum2[(i >> 1) & 1], pp);
+              const __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
+              const uint32_t hw = *reinterpret_cast<const uint32_t*>(&pb);
+              pw[i / 2] = hw;
+              if constexpr (kSplitP) {
+                // pp - bf16(pp) is exact in fp32; its bf16 rounding carries the next 8 bits
+                const float2 hi = make_float2(__uint_as_float(hw << 16), __uint_as_float(hw & 0xFFFF0000u));
+                const float2 d = __fadd2_rn(pp, make_float2(-hi.x, -hi.y));
+                const __nv_bfloat162 lb = __floats2bfloat162_rn(d.x, d.y);
+                lw[i / 2] = *reinterpret_cast<const uint32_t*>(&lb);
+              }
+            }
+            // P as bf16 pairs along keys: high part in columns [0, 64), low part in [64, 128)
+            tmem_st16(s_tm + ch * 32 + c / 2, pw);
+            if constexpr (kSplitP) tmem_st16(s_tm + 64 + ch * 32 + c / 2, lw);
+          }
+          l_part[t] = l_part[t] * corr + ((sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y));
+          tmem_wait_st();
+          if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+            // O_t must hold PV_t(j-1) before it is rescaled
+            if (!__all_sync(0xffffffffu, wait_or_abort(&bars->o_full[t], (j - 1) & 1, abort))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+  #pragma unroll
+            for (int c = 0; c < 64; c += 32) {
+              float ov[32];
+              tmem_ld32(o_tm + c, ov);
+              tmem_wait_ld();
+              uint32_t ow[32];
+  #pragma unroll
+              for (int i = 0; i < 32; ++i) ow[i] = __float_as_uint(ov[i] * corr);
+              tmem_st32(o_tm + c, ow);
+            }
+            tmem_wait_st();
+          }
+          m_ref[t] = m_new;
+          tc_fence_before();
+          mbar_arrive(&bars->p_full[t]);
+        }
+      }
+      // epilogue: O_t / l -> bf16 (l = the pair's two partial sums)
+  #pragma unroll
+      for (int t = 0; ok && t < 2; ++t, ++step) {
+        if (!__all_sync(0xffffffffu, wait_or_abort(&bars->o_full[t], (ntiles - 1) & 1, abort))) break;
+        tc_fence_after();
+        float* lbuf = red + (step & 1) * 2 * kTileM;
+        lbuf[ch * kTileM + r] = l_part[t];
+        asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+        const float l_tot = lbuf[r] + lbuf[kTileM + r];
+        const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
+        const int q_row = q0 + t * kTileM + r;
         const uint32_t o_tm = tmem + lane_off + 256 + t * 128 + ch * 64;
+        uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh + ch * 64;
+  #pragma unroll
+        for (int c = 0; c < 64; c += 32) {
+          float ov[32];
+          tmem_ld32(o_tm + c, ov);
+          tmem_wait_ld();
+          if (q_row < a.n_q) {
+  #pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 w;
+              w.x = pack2_bf16(ov[i] * inv, ov[i + 1] * inv);
+              w.y = pack2_bf16(ov[i + 2] * inv, ov[i + 3] * inv);
+              w.z = pack2_bf16(ov[i + 4] * inv, ov[i + 5] * inv);
+              w.w = pack2_bf16(ov[i + 6] * inv, ov[i + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + c + i) = w;
+            }
+          }
+        }
+      }
+    } else {
+      const int t = warp >> 2;             // query tile
+      const int quarter = warp & 3;        // TMEM lane quarter
+      const int r = quarter * 32 + lane;   // row within the tile
+      const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+      const uint32_t s_tm = tmem + lane_off + t * 128;
+      const uint32_t o_tm = tmem + lane_off + 256 + t * 128;
+      const int q_row = q0 + t * kTileM + r;
+      const long long vis_row = a.causal ? min((long long)kv_len, (long long)q_off + q_row + 1) : (long long)kv_len;
+      const long long vis_min =
+          a.causal ? min((long long)kv_len, (long long)q_off + q0 + t * kTileM + 1) : (long long)kv_len;
+      float m_ref = -INFINITY, l_run = 0.f;
+      bool ok = true;
+      for (int j = 0; j < ntiles; ++j) {
         if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[t], j & 1, abort))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        float sv[64];
-        tmem_ld32(s_tm + ch * 64, sv);
-        tmem_ld32(s_tm + ch * 64 + 32, sv + 32);
+        float sv[128];
+  #pragma unroll
+        for (int c = 0; c < 128; c += 32) tmem_ld32(s_tm + c, sv + c);
         tmem_wait_ld();
-        if ((long long)(j + 1) * kTileN > vis_min[t]) {
-          const long long vis = vis_row[t] - (long long)j * kTileN - ch * 64;  // visible columns of this half
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
+        if ((long long)(j + 1) * kTileN > vis_min) {
+          const long long vis = vis_row - (long long)j * kTileN;
+  #pragma unroll
+          for (int c = 0; c < 128; ++c)
             if (c >= vis) sv[c] = -INFINITY;
         }
-        // three-input max.f32 (sm_100): two new scores per instruction, 4 chains
-        float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
-#pragma unroll
-        for (int c = 4; c < 64; c += 2)
-          asm("max.f32 %0, %0, %1, %2;" : "+f"(mx4[(c >> 1) & 3]) : "f"(sv[c]), "f"(sv[c + 1]));
-        float* rbuf = red + (step & 1) * 2 * kTileM;
-        rbuf[ch * kTileM + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-        asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
-        const float mx = fmaxf(rbuf[r], rbuf[kTileM + r]);
-        const float m_tile = mx * a.scale_log2;  // scale > 0 keeps the order
-        const bool move = m_tile > m_ref[t] + kRescaleThreshold || (m_ref[t] == -INFINITY && m_tile != -INFINITY);
-        const float m_new = move ? m_tile : m_ref[t];
-        const float corr = move ? exp2f(m_ref[t] - m_new) : 1.f;
+        // eight independent max / sum chains instead of one 128-long chain
+        // three-input max.f32 (sm_100): two new scores per instruction
+        float mx8[8];
+  #pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+  #pragma unroll
+        for (int c = 8; c < 128; c += 2)
+          asm("max.f32 %0, %0, %1, %2;" : "+f"(mx8[(c >> 1) & 7]) : "f"(sv[c]), "f"(sv[c + 1]));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float m_tile = mx * a.scale_log2;
+        const bool move = m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY);
+        const float m_new = move ? m_tile : m_ref;
+        const float corr = move ? exp2f(m_ref - m_new) : 1.f;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        // packed fp32 pairs: scale-and-shift, sum and the split residual each
-        // take one FFMA2 / FADD2 per two scores; exp2 is the MUFU instruction
+        // packed fp32 pairs: scale-and-shift, sum and the split residual each take
+        // one FFMA2 / FADD2 per two scores; exp2 is the MUFU instruction
         // (ex2.approx, relative error ~2^-22, far below the 2^-16 of split P)
-        float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        float2 sum4[4];
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) sum4[i] = make_float2(0.f, 0.f);
         const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
         const float2 nm2 = make_float2(-m_use, -m_use);
-#pragma unroll
-        for (int c = 0; c < 64; c += 32) {
+  #pragma unroll
+        for (int c = 0; c < 128; c += 32) {
           uint32_t pw[16];
           uint32_t lw[kSplitP ? 16 : 1];
-#pragma unroll
+  #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const float2 x = __ffma2_rn(make_float2(sv[c + i], sv[c + i + 1]), sc2, nm2);
             float2 pp;
             asm("ex2.approx.f32 %0, %1;" : "=f"(pp.x) : "f"(x.x));
             asm("ex2.approx.f32 %0, %1;" : "=f"(pp.y) : "f"(x.y));
-            sum2[(i >> 1) & 1] = __fadd2_rn(sum2[(i >> 1) & 1], pp);
+            sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], pp);
             const __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
             const uint32_t hw = *reinterpret_cast<const uint32_t*>(&pb);
             pw[i / 2] = hw;
@@ -332,11 +468,13 @@ __global__ void __launch_bounds__(kPPThreads, 1)
               lw[i / 2] = *reinterpret_cast<const uint32_t*>(&lb);
             }
           }
-          // P as bf16 pairs along keys: high part in columns [0, 64), low part in [64, 128)
-          tmem_st16(s_tm + ch * 32 + c / 2, pw);
-          if constexpr (kSplitP) tmem_st16(s_tm + 64 + ch * 32 + c / 2, lw);
+          // P_j as bf16 pairs along keys: high part in columns [0, 64), low part in [64, 128)
+          tmem_st16(s_tm + c / 2, pw);
+          if constexpr (kSplitP) tmem_st16(s_tm + 64 + c / 2, lw);
         }
-        l_part[t] = l_part[t] * corr + ((sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y));
+        const float sum = ((sum4[0].x + sum4[0].y) + (sum4[1].x + sum4[1].y)) +
+                          ((sum4[2].x + sum4[2].y) + (sum4[3].x + sum4[3].y));
+        l_run = l_run * corr + sum;
         tmem_wait_st();
         if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
           // O_t must hold PV_t(j-1) before it is rescaled
@@ -345,50 +483,42 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             break;
           }
           tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < 64; c += 32) {
+  #pragma unroll
+          for (int c = 0; c < 128; c += 32) {
             float ov[32];
             tmem_ld32(o_tm + c, ov);
             tmem_wait_ld();
             uint32_t ow[32];
-#pragma unroll
+  #pragma unroll
             for (int i = 0; i < 32; ++i) ow[i] = __float_as_uint(ov[i] * corr);
             tmem_st32(o_tm + c, ow);
           }
           tmem_wait_st();
         }
-        m_ref[t] = m_new;
+        m_ref = m_new;
         tc_fence_before();
         mbar_arrive(&bars->p_full[t]);
       }
-    }
-    // epilogue: O_t / l -> bf16 (l = the pair's two partial sums)
-#pragma unroll
-    for (int t = 0; ok && t < 2; ++t, ++step) {
-      if (!__all_sync(0xffffffffu, wait_or_abort(&bars->o_full[t], (ntiles - 1) & 1, abort))) break;
-      tc_fence_after();
-      float* lbuf = red + (step & 1) * 2 * kTileM;
-      lbuf[ch * kTileM + r] = l_part[t];
-      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
-      const float l_tot = lbuf[r] + lbuf[kTileM + r];
-      const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
-      const int q_row = q0 + t * kTileM + r;
-      const uint32_t o_tm = tmem + lane_off + 256 + t * 128 + ch * 64;
-      uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh + ch * 64;
-#pragma unroll
-      for (int c = 0; c < 64; c += 32) {
-        float ov[32];
-        tmem_ld32(o_tm + c, ov);
-        tmem_wait_ld();
-        if (q_row < a.n_q) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w;
-            w.x = pack2_bf16(ov[i] * inv, ov[i + 1] * inv);
-            w.y = pack2_bf16(ov[i + 2] * inv, ov[i + 3] * inv);
-            w.z = pack2_bf16(ov[i + 4] * inv, ov[i + 5] * inv);
-            w.w = pack2_bf16(ov[i + 6] * inv, ov[i + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + c + i) = w;
+      // epilogue: O_t / l -> bf16
+      if (ok && __all_sync(0xffffffffu, wait_or_abort(&bars->o_full[t], (ntiles - 1) & 1, abort))) {
+        tc_fence_after();
+        const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
+        uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh;
+  #pragma unroll
+        for (int c = 0; c < 128; c += 32) {
+          float ov[32];
+          tmem_ld32(o_tm + c, ov);
+          tmem_wait_ld();
+          if (q_row < a.n_q) {
+  #pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 w;
+              w.x = pack2_bf16(ov[i] * inv, ov[i + 1] * inv);
+              w.y = pack2_bf16(ov[i + 2] * inv, ov[i + 3] * inv);
+              w.z = pack2_bf16(ov[i + 4] * inv, ov[i + 5] * inv);
+              w.w = pack2_bf16(ov[i + 6] * inv, ov[i + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + c + i) = w;
+            }
           }
         }
       }
@@ -486,16 +616,18 @@ cudaError_t prefill_tc_launch(const PrefillTcParams& p, cudaStream_t stream) {
   a.scale_log2 = p.scale_log2;
   a.status = p.status;
   dim3 grid2(p.n_q_heads, (p.n_q + 2 * kTileM - 1) / (2 * kTileM), p.batch);
+  // split P: two softmax threads per row (one per row would spill); bf16 P:
+  // one thread per row, warps 0-3 on tile A and 4-7 on tile B
   if (p.split_p) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_pp_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kPPSmemAlloc);
+    cudaError_t e = cudaFuncSetAttribute(prefill_pp_kernel<true, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPPSmemAlloc);
     if (e != cudaSuccess) return e;
-    prefill_pp_kernel<true><<<grid2, kPPThreads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
+    prefill_pp_kernel<true, true><<<grid2, kPPThreads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
   } else {
-    cudaError_t e = cudaFuncSetAttribute(prefill_pp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kPPSmemAlloc);
+    cudaError_t e = cudaFuncSetAttribute(prefill_pp_kernel<false, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPPSmemAlloc);
     if (e != cudaSuccess) return e;
-    prefill_pp_kernel<false><<<grid2, kPPThreads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
+    prefill_pp_kernel<false, false><<<grid2, kPPThreads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
   }
   return cudaGetLastError();
 }
