@@ -261,19 +261,25 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
       const int pair_bar = 1 + quarter;
       float* red = reinterpret_cast<float*>(smem + kPPRedOff);  // [parity][half][row]
-      float m_ref[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.f, 0.f};
-      long long vis_row[2], vis_min[2];
-  #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int q_row = q0 + t * kTileM + r;
-        vis_row[t] = a.causal ? min((long long)kv_len, (long long)q_off + q_row + 1) : (long long)kv_len;
-        vis_min[t] = a.causal ? min((long long)kv_len, (long long)q_off + q0 + t * kTileM + 1) : (long long)kv_len;
-      }
+      // Per-tile state in scalars selected by the tile index: the tile loop
+      // below is not unrolled, so one copy of its body serves both tiles and
+      // the kernel's hot code stays small enough for the instruction cache.
+      float m_ref0 = -INFINITY, m_ref1 = -INFINITY, l_part0 = 0.f, l_part1 = 0.f;
+      const long long vis_row0 =
+          a.causal ? min((long long)kv_len, (long long)q_off + q0 + r + 1) : (long long)kv_len;
+      const long long vis_row1 =
+          a.causal ? min((long long)kv_len, (long long)q_off + q0 + kTileM + r + 1) : (long long)kv_len;
+      const long long vis_min0 = a.causal ? min((long long)kv_len, (long long)q_off + q0 + 1) : (long long)kv_len;
+      const long long vis_min1 =
+          a.causal ? min((long long)kv_len, (long long)q_off + q0 + kTileM + 1) : (long long)kv_len;
       bool ok = true;
       int step = 0;  // parity of the exchange buffer
       for (int j = 0; ok && j < ntiles; ++j) {
-  #pragma unroll
+  #pragma unroll 1
         for (int t = 0; t < 2; ++t, ++step) {
+          const float m_ref_t = t ? m_ref1 : m_ref0;
+          const long long vis_row_t = t ? vis_row1 : vis_row0;
+          const long long vis_min_t = t ? vis_min1 : vis_min0;
           const uint32_t s_tm = tmem + lane_off + t * 128;
           const uint32_t o_tm = tmem + lane_off + 256 + t * 128 + ch * 64;
           if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[t], j & 1, abort))) {
@@ -285,8 +291,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           tmem_ld32(s_tm + ch * 64, sv);
           tmem_ld32(s_tm + ch * 64 + 32, sv + 32);
           tmem_wait_ld();
-          if ((long long)(j + 1) * kTileN > vis_min[t]) {
-            const long long vis = vis_row[t] - (long long)j * kTileN - ch * 64;  // visible columns of this half
+          if ((long long)(j + 1) * kTileN > vis_min_t) {
+            const long long vis = vis_row_t - (long long)j * kTileN - ch * 64;  // visible columns of this half
   #pragma unroll
             for (int c = 0; c < 64; ++c)
               if (c >= vis) sv[c] = -INFINITY;
@@ -301,9 +307,9 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
           const float mx = fmaxf(rbuf[r], rbuf[kTileM + r]);
           const float m_tile = mx * a.scale_log2;  // scale > 0 keeps the order
-          const bool move = m_tile > m_ref[t] + kRescaleThreshold || (m_ref[t] == -INFINITY && m_tile != -INFINITY);
-          const float m_new = move ? m_tile : m_ref[t];
-          const float corr = move ? exp2f(m_ref[t] - m_new) : 1.f;
+          const bool move = m_tile > m_ref_t + kRescaleThreshold || (m_ref_t == -INFINITY && m_tile != -INFINITY);
+          const float m_new = move ? m_tile : m_ref_t;
+          const float corr = move ? exp2f(m_ref_t - m_new) : 1.f;
           const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
           // packed fp32 pairs: scale-and-shift, sum and the split residual each
           // take one FFMA2 / FADD2 per two scores; exp2 is the MUFU instruction
@@ -337,7 +343,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             tmem_st16(s_tm + ch * 32 + c / 2, pw);
             if constexpr (kSplitP) tmem_st16(s_tm + 64 + ch * 32 + c / 2, lw);
           }
-          l_part[t] = l_part[t] * corr + ((sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y));
+          const float l_new = (t ? l_part1 : l_part0) * corr + ((sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y));
+          if (t) l_part1 = l_new; else l_part0 = l_new;
           tmem_wait_st();
           if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
             // O_t must hold PV_t(j-1) before it is rescaled
@@ -358,18 +365,18 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             }
             tmem_wait_st();
           }
-          m_ref[t] = m_new;
+          if (t) m_ref1 = m_new; else m_ref0 = m_new;
           tc_fence_before();
           mbar_arrive(&bars->p_full[t]);
         }
       }
       // epilogue: O_t / l -> bf16 (l = the pair's two partial sums)
-  #pragma unroll
+  #pragma unroll 1
       for (int t = 0; ok && t < 2; ++t, ++step) {
         if (!__all_sync(0xffffffffu, wait_or_abort(&bars->o_full[t], (ntiles - 1) & 1, abort))) break;
         tc_fence_after();
         float* lbuf = red + (step & 1) * 2 * kTileM;
-        lbuf[ch * kTileM + r] = l_part[t];
+        lbuf[ch * kTileM + r] = t ? l_part1 : l_part0;
         asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
         const float l_tot = lbuf[r] + lbuf[kTileM + r];
         const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
