@@ -84,11 +84,19 @@ constexpr int kPPQOff = 0;                                  // Q_A, then Q_B
 constexpr int kPPKOff = 2 * kTileBytes;
 constexpr int kPPVOff = kPPKOff + kPPStages * kTileBytes;
 constexpr int kPPBarOff = kPPVOff + kPPStages * kTileBytes;
-constexpr int kPPRedOff = kPPBarOff + 256;                   // row max / sum exchange [2][2][128] floats
-constexpr int kPPSmemAlloc = kPPRedOff + 2 * 2 * kTileM * 4 + 1024;
-constexpr int kPPMmaWarp = 8;
-constexpr int kPPTmaWarp = 9;
-constexpr int kPPThreads = 10 * 32;
+constexpr int kPPRedOff = kPPBarOff + 256;                   // row max / sum exchange [2][<= 4][128] floats
+constexpr int kPPSmemAlloc = kPPRedOff + 2 * 4 * kTileM * 4 + 1024;
+
+// Warp roles for kRowThreads softmax threads per query row: 1 (warps 0-3 on
+// tile A, 4-7 on tile B), 2 (8 warps, both tiles in turn) or 4 (16 warps);
+// the MMA and TMA warps follow the softmax warps.
+template <int kRowThreads>
+struct PPLayout {
+  static constexpr int kSoftmaxWarps = kRowThreads == 4 ? 16 : 8;
+  static constexpr int kMmaWarp = kSoftmaxWarps;
+  static constexpr int kTmaWarp = kSoftmaxWarps + 1;
+  static constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
+};
 
 struct PPBars {
   uint64_t q_full;
@@ -104,8 +112,8 @@ struct PPBars {
 };
 static_assert(sizeof(PPBars) <= 256, "barrier block");
 
-template <bool kSplitP, bool kPairRows>
-__global__ void __launch_bounds__(kPPThreads, 1)
+template <bool kSplitP, int kRowThreads>
+__global__ void __launch_bounds__(PPLayout<kRowThreads>::kThreads, 1)
     prefill_pp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -148,7 +156,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->s_full[t], 1);
-      mbar_init(&bars->p_full[t], kPairRows ? 8 * 32 : kTileM);
+      mbar_init(&bars->p_full[t], kRowThreads > 1 ? PPLayout<kRowThreads>::kSoftmaxWarps * 32 : kTileM);
       mbar_init(&bars->o_full[t], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -156,7 +164,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     bars->issued = 0;
     mbar_fence_init();
   }
-  if (warp == kPPMmaWarp) {
+  if (warp == PPLayout<kRowThreads>::kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&bars->tmem_base)),
                  "r"(kTmemCols)
                  : "memory");
@@ -167,7 +175,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == kPPTmaWarp) {
+  if (warp == PPLayout<kRowThreads>::kTmaWarp) {
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
       uint8_t* q_smem = smem + kPPQOff;
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
         bars->issued = j + 1;
       }
     }
-  } else if (warp == kPPMmaWarp) {
+  } else if (warp == PPLayout<kRowThreads>::kMmaWarp) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       const uint32_t id_s = idesc_bf16(kTileM, kTileN, 0);
@@ -250,17 +258,20 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    if constexpr (kPairRows) {
-      // All 8 warps take tile A then tile B: two threads per query row (warps
-      // w and w + 4 share a TMEM lane quarter), each owning 64 of the 128
-      // columns; the pair exchanges row maxima (and, at the end, row sums)
-      // through shared memory under a 64-thread named barrier.
+    if constexpr (kRowThreads > 1) {
+      // All softmax warps take tile A then tile B: kRowThreads threads per
+      // query row (warps w, w + 4, ... share a TMEM lane quarter), each owning
+      // CW of the 128 columns; they exchange row maxima (and, at the end, row
+      // sums) through shared memory under a named barrier of the row group.
+      constexpr int RT = kRowThreads;
+      constexpr int CW = 128 / RT;         // columns per thread
       const int quarter = warp & 3;
-      const int ch = warp >> 2;            // column half
+      const int ch = warp >> 2;            // column slice
       const int r = quarter * 32 + lane;   // row within a tile
       const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
       const int pair_bar = 1 + quarter;
-      float* red = reinterpret_cast<float*>(smem + kPPRedOff);  // [parity][half][row]
+      const int bar_threads = 32 * RT;
+      float* red = reinterpret_cast<float*>(smem + kPPRedOff);  // [parity][slice][row]
       // Per-tile state in scalars selected by the tile index: the tile loop
       // below is not unrolled, so one copy of its body serves both tiles and
       // the kernel's hot code stays small enough for the instruction cache.
@@ -281,31 +292,33 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           const long long vis_row_t = t ? vis_row1 : vis_row0;
           const long long vis_min_t = t ? vis_min1 : vis_min0;
           const uint32_t s_tm = tmem + lane_off + t * 128;
-          const uint32_t o_tm = tmem + lane_off + 256 + t * 128 + ch * 64;
+          const uint32_t o_tm = tmem + lane_off + 256 + t * 128 + ch * CW;
           if (!__all_sync(0xffffffffu, wait_or_abort(&bars->s_full[t], j & 1, abort))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          float sv[64];
-          tmem_ld32(s_tm + ch * 64, sv);
-          tmem_ld32(s_tm + ch * 64 + 32, sv + 32);
+          float sv[CW];
+  #pragma unroll
+          for (int c = 0; c < CW; c += 32) tmem_ld32(s_tm + ch * CW + c, sv + c);
           tmem_wait_ld();
           if ((long long)(j + 1) * kTileN > vis_min_t) {
-            const long long vis = vis_row_t - (long long)j * kTileN - ch * 64;  // visible columns of this half
+            const long long vis = vis_row_t - (long long)j * kTileN - ch * CW;  // visible columns of this slice
   #pragma unroll
-            for (int c = 0; c < 64; ++c)
+            for (int c = 0; c < CW; ++c)
               if (c >= vis) sv[c] = -INFINITY;
           }
           // three-input max.f32 (sm_100): two new scores per instruction, 4 chains
           float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
   #pragma unroll
-          for (int c = 4; c < 64; c += 2)
+          for (int c = 4; c < CW; c += 2)
             asm("max.f32 %0, %0, %1, %2;" : "+f"(mx4[(c >> 1) & 3]) : "f"(sv[c]), "f"(sv[c + 1]));
-          float* rbuf = red + (step & 1) * 2 * kTileM;
+          float* rbuf = red + (step & 1) * RT * kTileM;
           rbuf[ch * kTileM + r] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-          asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
-          const float mx = fmaxf(rbuf[r], rbuf[kTileM + r]);
+          asm volatile("bar.sync %0, %1;" ::"r"(pair_bar), "r"(bar_threads) : "memory");
+          float mx = rbuf[r];
+  #pragma unroll
+          for (int c2 = 1; c2 < RT; ++c2) mx = fmaxf(mx, rbuf[c2 * kTileM + r]);
           const float m_tile = mx * a.scale_log2;  // scale > 0 keeps the order
           const bool move = m_tile > m_ref_t + kRescaleThreshold || (m_ref_t == -INFINITY && m_tile != -INFINITY);
           const float m_new = move ? m_tile : m_ref_t;
@@ -318,7 +331,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
           const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
           const float2 nm2 = make_float2(-m_use, -m_use);
   #pragma unroll
-          for (int c = 0; c < 64; c += 32) {
+          for (int c = 0; c < CW; c += 32) {
             uint32_t pw[16];
             uint32_t lw[kSplitP ? 16 : 1];
   #pragma unroll
@@ -340,8 +353,8 @@ __global__ void __launch_bounds__(kPPThreads, 1)
               }
             }
             // P as bf16 pairs along keys: high part in columns [0, 64), low part in [64, 128)
-            tmem_st16(s_tm + ch * 32 + c / 2, pw);
-            if constexpr (kSplitP) tmem_st16(s_tm + 64 + ch * 32 + c / 2, lw);
+            tmem_st16(s_tm + ch * (CW / 2) + c / 2, pw);
+            if constexpr (kSplitP) tmem_st16(s_tm + 64 + ch * (CW / 2) + c / 2, lw);
           }
           const float l_new = (t ? l_part1 : l_part0) * corr + ((sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y));
           if (t) l_part1 = l_new; else l_part0 = l_new;
@@ -354,7 +367,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
             }
             tc_fence_after();
   #pragma unroll
-            for (int c = 0; c < 64; c += 32) {
+            for (int c = 0; c < CW; c += 32) {
               float ov[32];
               tmem_ld32(o_tm + c, ov);
               tmem_wait_ld();
@@ -375,16 +388,18 @@ __global__ void __launch_bounds__(kPPThreads, 1)
       for (int t = 0; ok && t < 2; ++t, ++step) {
         if (!__all_sync(0xffffffffu, wait_or_abort(&bars->o_full[t], (ntiles - 1) & 1, abort))) break;
         tc_fence_after();
-        float* lbuf = red + (step & 1) * 2 * kTileM;
+        float* lbuf = red + (step & 1) * RT * kTileM;
         lbuf[ch * kTileM + r] = t ? l_part1 : l_part0;
-        asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
-        const float l_tot = lbuf[r] + lbuf[kTileM + r];
+        asm volatile("bar.sync %0, %1;" ::"r"(pair_bar), "r"(bar_threads) : "memory");
+        float l_tot = lbuf[r];
+  #pragma unroll
+        for (int c2 = 1; c2 < RT; ++c2) l_tot += lbuf[c2 * kTileM + r];
         const float inv = (l_tot > 0.f) ? 1.f / l_tot : 0.f;
         const int q_row = q0 + t * kTileM + r;
-        const uint32_t o_tm = tmem + lane_off + 256 + t * 128 + ch * 64;
-        uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh + ch * 64;
+        const uint32_t o_tm = tmem + lane_off + 256 + t * 128 + ch * CW;
+        uint16_t* dst = a.o + b * a.o_sb + (long long)q_row * a.o_sr + (long long)h * a.o_sh + ch * CW;
   #pragma unroll
-        for (int c = 0; c < 64; c += 32) {
+        for (int c = 0; c < CW; c += 32) {
           float ov[32];
           tmem_ld32(o_tm + c, ov);
           tmem_wait_ld();
@@ -536,7 +551,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
   __syncthreads();
   if (*abort) {
     if (threadIdx.x == 0) atomicOr(a.status, kDevWaitTimeout);
-    if (threadIdx.x == kPPTmaWarp * 32) {
+    if (threadIdx.x == PPLayout<kRowThreads>::kTmaWarp * 32) {
       (void)mbar_wait_bounded(&bars->q_full, 0);
       const int issued = bars->issued;
       for (int j = (issued > kPPStages ? issued - kPPStages : 0); j < issued; ++j)
@@ -544,7 +559,7 @@ __global__ void __launch_bounds__(kPPThreads, 1)
     }
   }
   __syncthreads();
-  if (warp == kPPMmaWarp) {
+  if (warp == PPLayout<kRowThreads>::kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
@@ -623,19 +638,22 @@ cudaError_t prefill_tc_launch(const PrefillTcParams& p, cudaStream_t stream) {
   a.scale_log2 = p.scale_log2;
   a.status = p.status;
   dim3 grid2(p.n_q_heads, (p.n_q + 2 * kTileM - 1) / (2 * kTileM), p.batch);
-  // split P: two softmax threads per row (one per row would spill); bf16 P:
+  // split P: several softmax threads per row (one per row would spill); bf16 P:
   // one thread per row, warps 0-3 on tile A and 4-7 on tile B
+  auto launch = [&](auto kernel, int threads) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPPSmemAlloc);
+    if (e != cudaSuccess) return e;
+    kernel<<<grid2, threads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
+    return cudaSuccess;
+  };
+  cudaError_t e;
   if (p.split_p) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_pp_kernel<true, true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPPSmemAlloc);
-    if (e != cudaSuccess) return e;
-    prefill_pp_kernel<true, true><<<grid2, kPPThreads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
+    // two threads per row: four (16 softmax warps) measured 761 vs 773 TFLOP/s on config 5
+    e = launch(prefill_pp_kernel<true, 2>, PPLayout<2>::kThreads);
   } else {
-    cudaError_t e = cudaFuncSetAttribute(prefill_pp_kernel<false, false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPPSmemAlloc);
-    if (e != cudaSuccess) return e;
-    prefill_pp_kernel<false, false><<<grid2, kPPThreads, kPPSmemAlloc, stream>>>(mq, mk, mv, a);
+    e = launch(prefill_pp_kernel<false, 1>, PPLayout<1>::kThreads);
   }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
