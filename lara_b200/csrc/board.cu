@@ -391,6 +391,7 @@ bool g_tables_ready[64] = {};
 extern "C" int lara_attention_dense_board(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
                                           int n_q_heads, int n_kv_heads, int head_dim, int seq_len, int causal,
                                           int q_pos_base, int kv_pos_base, void* stream) {
+  LARA_NVTX("lara_attention_dense_board");
   if (head_dim != kD)
     return lara::set_last_error(LARA_ERR_UNSUPPORTED, "board arithmetic is defined for head_dim 128 only");
   if (n_q_heads < 1 || n_kv_heads < 1 || n_q_heads % n_kv_heads || seq_len < 1)

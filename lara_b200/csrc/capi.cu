@@ -20,6 +20,7 @@
 
 using lara::DecodeParams;
 
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -376,6 +377,7 @@ int lara_gqa_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* 
                     uint16_t* o, int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len,
                     float scale, int num_splits, int chunk_tokens, void* workspace, size_t workspace_bytes,
                     void* stream) {
+  LARA_NVTX("lara_gqa_decode");
   if (!o) return fail(LARA_ERR_STREAM_DEST, "null output pointer");
   return decode_common(q, k_cache, v_cache, seq_lens, o, nullptr, nullptr, batch, n_q_heads, n_kv_heads, head_dim,
                        max_seq_len, scale, num_splits, chunk_tokens, workspace, workspace_bytes, stream);
@@ -385,6 +387,7 @@ int lara_gqa_decode_partial(const uint16_t* q, const uint16_t* k_cache, const ui
                             const int32_t* seq_lens, float* part_ml, float* part_acc, int batch, int n_q_heads,
                             int n_kv_heads, int head_dim, int max_seq_len, float scale, int num_splits,
                             int chunk_tokens, void* workspace, size_t workspace_bytes, void* stream) {
+  LARA_NVTX("lara_gqa_decode_partial");
   if (!part_ml || !part_acc) return fail(LARA_ERR_STREAM_DEST, "null partial output pointer");
   return decode_common(q, k_cache, v_cache, seq_lens, nullptr, part_ml, part_acc, batch, n_q_heads, n_kv_heads,
                        head_dim, max_seq_len, scale, num_splits, chunk_tokens, workspace, workspace_bytes, stream);
@@ -392,6 +395,7 @@ int lara_gqa_decode_partial(const uint16_t* q, const uint16_t* k_cache, const ui
 
 int lara_lse_combine(const float* part_ml, const float* part_acc, int num_parts, int rows, int head_dim, uint16_t* o,
                      void* stream) {
+  LARA_NVTX("lara_lse_combine");
   if (!part_ml || !part_acc || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
   if (num_parts < 1 || rows < 1 || head_dim < 2 || head_dim % 2)
     return fail(LARA_ERR_BAD_CFG, "num_parts, rows must be >= 1 and head_dim even");
@@ -422,6 +426,7 @@ int lara_lse_combine_strided(const float* part_ml, long long ml_part_stride, con
 int lara_kv_append(uint16_t* k_cache, uint16_t* v_cache, int32_t* seq_lens, const uint16_t* k_new,
                    const uint16_t* v_new, int batch, int n_kv_heads, int head_dim, int max_seq_len, int n_new,
                    void* workspace, void* stream) {
+  LARA_NVTX("lara_kv_append");
   if (!k_cache || !v_cache || !seq_lens || !k_new || !v_new) return fail(LARA_ERR_STREAM_DEST, "null pointer");
   if (batch < 1 || n_kv_heads < 1 || head_dim < 8 || head_dim % 8 || max_seq_len < 1 || n_new < 0)
     return fail(LARA_ERR_BAD_CFG, "bad append geometry");
@@ -438,6 +443,7 @@ int lara_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pages, const uint
                           const int32_t* block_table, const int32_t* seq_lens, uint16_t* o, int batch, int n_q_heads,
                           int n_kv_heads, int head_dim, int page_size, int pages_per_seq, int num_pages, float scale,
                           int num_splits, int chunk_tokens, void* workspace, size_t workspace_bytes, void* stream) {
+  LARA_NVTX("lara_gqa_decode_paged");
   int page_log2 = 0;
   int rc = check_paged(page_size, pages_per_seq, num_pages, &page_log2);
   if (rc) return rc;
@@ -450,6 +456,7 @@ int lara_gqa_decode_paged(const uint16_t* q, const uint16_t* k_pages, const uint
 int lara_kv_append_paged(uint16_t* k_pages, uint16_t* v_pages, const int32_t* block_table, int32_t* seq_lens,
                          const uint16_t* k_new, const uint16_t* v_new, int batch, int n_kv_heads, int head_dim,
                          int page_size, int pages_per_seq, int num_pages, int n_new, void* workspace, void* stream) {
+  LARA_NVTX("lara_kv_append_paged");
   if (!k_pages || !v_pages || !block_table || !seq_lens || !k_new || !v_new)
     return fail(LARA_ERR_STREAM_DEST, "null pointer");
   int page_log2 = 0;
@@ -487,6 +494,7 @@ size_t lara_prefill_workspace_bytes(int batch, int n_new, int n_q_heads, int n_k
 int lara_gqa_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* cached_lens,
                      uint16_t* o, int batch, int n_new, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len,
                      int causal, float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  LARA_NVTX("lara_gqa_prefill");
   return prefill_common(q, k_cache, v_cache, cached_lens, o, batch, n_new, n_q_heads, n_kv_heads, head_dim,
                         max_seq_len, causal, scale, workspace, workspace_bytes, stream);
 }
@@ -500,6 +508,7 @@ size_t lara_dense_workspace_bytes(int n_q_heads, int n_kv_heads, int head_dim, i
 int lara_attention_dense(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o, int n_q_heads,
                          int n_kv_heads, int head_dim, int seq_len, int q_pos_base, int kv_pos_base, int causal,
                          float scale, void* workspace, size_t workspace_bytes, void* stream) {
+  LARA_NVTX("lara_attention_dense");
   if (!(scale > 0.f) || !std::isfinite(scale)) return fail(LARA_ERR_BAD_CFG, "scale must be positive and finite");
   return dense_common(q, k, v, o, n_q_heads, n_kv_heads, head_dim, seq_len, q_pos_base, kv_pos_base, causal, scale,
                       workspace, workspace_bytes, stream);
@@ -746,6 +755,7 @@ int lara_configure(lara_ctx* c, int seq_len, int q_pos_base, int kv_pos_base, in
 }
 
 int lara_kv_load(lara_ctx* c, const uint16_t* k, const uint16_t* v, const int32_t* lens, int src_len, int on_device) {
+  LARA_NVTX("lara_kv_load");
   int rc = ctx_check(c);
   if (rc) return rc;
   if (!k || !v || !lens) return fail(LARA_ERR_STREAM_DEST, "null pointer");
@@ -807,6 +817,7 @@ int lara_kv_append_ctx(lara_ctx* c, const uint16_t* k_new, const uint16_t* v_new
 
 int lara_run_prefill_chunk(lara_ctx* c, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new, uint16_t* o,
                            int n_new, int causal, int on_device) {
+  LARA_NVTX("lara_run_prefill_chunk");
   int rc = ctx_check(c);
   if (rc) return rc;
   if (!q || !k_new || !v_new || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
@@ -874,6 +885,7 @@ int lara_run_prefill_chunk(lara_ctx* c, const uint16_t* q, const uint16_t* k_new
 }
 
 int lara_kv_read(lara_ctx* c, uint16_t* k, uint16_t* v, int32_t* lens_out, int dst_len, int on_device) {
+  LARA_NVTX("lara_kv_read");
   int rc = ctx_check(c);
   if (rc) return rc;
   if (!k || !v || !lens_out) return fail(LARA_ERR_STREAM_DEST, "null pointer");
@@ -901,6 +913,7 @@ int lara_get_seq_lens(lara_ctx* c, int32_t* lens_out) {
 }
 
 int lara_run_query(lara_ctx* c, const uint16_t* q, uint16_t* o, int on_device) {
+  LARA_NVTX("lara_run_query");
   int rc = ctx_check(c);
   if (rc) return rc;
   if (!q || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
@@ -944,6 +957,7 @@ int lara_run_query(lara_ctx* c, const uint16_t* q, uint16_t* o, int on_device) {
 
 int lara_run_attention(lara_ctx* c, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
                        int on_device) {
+  LARA_NVTX("lara_run_attention");
   int rc = ctx_check(c);
   if (rc) return rc;
   if (!q || !k || !v || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
@@ -1006,6 +1020,7 @@ int ensure_buf(void** p, size_t* cap, size_t need) {
 
 int lara_run_layer(lara_ctx* c, const uint16_t* x, const uint16_t* w_qkv, const uint16_t* rms_weight, int hidden,
                    uint16_t* o, float rms_eps, float rope_base, int on_device) {
+  LARA_NVTX("lara_run_layer");
   int rc = ctx_check(c);
   if (rc) return rc;
   if (!x || !w_qkv || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
@@ -1142,6 +1157,7 @@ int lara_sync(lara_ctx* c, int timeout_ms) {
 }
 
 int lara_decode(lara_ctx* c, const uint16_t* q, uint16_t* o, int splits, void* stream) {
+  LARA_NVTX("lara_decode");
   int rc = ctx_check(c);
   if (rc) return rc;
   if (!q || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");
@@ -1185,6 +1201,7 @@ int lara_decode(lara_ctx* c, const uint16_t* q, uint16_t* o, int splits, void* s
 
 int lara_prefill(lara_ctx* c, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new, uint16_t* o,
                  int n_new, int causal, void* stream) {
+  LARA_NVTX("lara_prefill");
   int rc = ctx_check(c);
   if (rc) return rc;
   if (!q || !k_new || !v_new || !o) return fail(LARA_ERR_STREAM_DEST, "null pointer");

@@ -7,6 +7,16 @@
 #include <string>
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
+
+// Named NVTX range around a C-ABI entry point, so profiler timelines show the
+// library's calls (NVTX v3 is header-only; without an attached tool a range
+// costs a null check).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+};
+#define LARA_NVTX(name) NvtxRange lara_nvtx_range_(name)
 
 namespace lara {
 

@@ -51,6 +51,7 @@ extern "C" int lara_gqa_decode_noalloc(const uint16_t* q, const uint16_t* k_cach
                                        const int32_t* seq_lens, uint16_t* o, int batch, int n_q_heads,
                                        int n_kv_heads, int head_dim, int max_seq_len, float scale, int num_splits,
                                        int chunk_tokens, void* stream) {
+  LARA_NVTX("lara_gqa_decode_noalloc");
   const size_t cap = LARA_NOALLOC_SCRATCH_BYTES;
   if (batch < 1 || n_q_heads < 1 || n_kv_heads < 1 || head_dim < 1 || max_seq_len < 1 ||
       n_q_heads % n_kv_heads != 0)

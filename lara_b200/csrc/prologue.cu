@@ -334,6 +334,7 @@ extern "C" int lara_layer_prologue(const uint16_t* x, const uint16_t* rms_weight
                                    uint16_t* k, uint16_t* v, int batch, int seq_len, int hidden, int n_q_heads,
                                    int n_kv_heads, int head_dim, int q_pos_base, int kv_pos_base, float rms_eps,
                                    float rope_base, void* workspace, size_t workspace_bytes, void* stream) {
+  LARA_NVTX("lara_layer_prologue");
   if (head_dim != kHead)
     return set_last_error(LARA_ERR_UNSUPPORTED, "the fused projection kernel is built for head_dim 128");
   if (batch < 1 || seq_len < 1 || hidden < kBK || hidden % kBK || n_q_heads < 1 || n_kv_heads < 1 ||
