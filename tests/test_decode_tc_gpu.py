@@ -252,3 +252,53 @@ def test_dense_transaction_on_decode_kernels(dev, monkeypatch, path):
     gold = oracle.cpu_attention_numpy(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7, n_q_heads=Hq,
                                       n_kv_heads=Hkv, head_dim=D)
     assert_bf16_parity(o, gold, what=f"dense {path}")
+
+
+def _list_schedule_plan(lens, L, hkv, sms, overhead=1.0):
+    """The planner's model restated: items in ticket order (split-major) go to the
+    earliest-free CTA; an item costs its 128-token tiles plus `overhead` tiles."""
+    import heapq
+
+    max_tiles = -(-L // 128)
+    best = None
+    c = 128
+    while True:
+        c = min(c, max_tiles * 128)
+        ns = -(-L // c)
+        heap = [0.0] * sms
+        for sp in range(ns):
+            for n in lens:
+                begin = sp * c
+                if n == 0 and sp == 0:
+                    for _ in range(hkv):
+                        heapq.heapreplace(heap, heap[0] + overhead)
+                    continue
+                if begin >= n:
+                    continue
+                cost = -(-min(c, n - begin) // 128) + overhead
+                for _ in range(hkv):
+                    heapq.heapreplace(heap, heap[0] + cost)
+        span = max(heap)
+        if best is None or span < best[0] * (1 - 1e-9):
+            best = (span, ns, c)
+        if c >= max_tiles * 128:
+            break
+        c *= 2
+    return best[1], best[2]
+
+
+def test_tc_plan_matches_list_schedule_model(tc):
+    import ctypes
+
+    from lara_b200 import _native
+    from lara_b200.workloads import CONFIGS
+
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    cases = [(CONFIGS[3].lens(), 32768), (CONFIGS[3].lens(16), 32535), (np.full(64, 4096), 4096),
+             (np.array([0, 5, 3000, 129]), 3000)]
+    for lens, L in cases:
+        lens = np.ascontiguousarray(lens, np.int32)
+        ns, ch = ctypes.c_int(0), ctypes.c_int(0)
+        _native.check(_native.lib.lara_decode_plan(len(lens), 64, 8, 128, L, lens.ctypes.data, ctypes.byref(ns),
+                                                    ctypes.byref(ch)), "plan")
+        assert (ns.value, ch.value) == _list_schedule_plan(lens.tolist(), L, 8, sms), (len(lens), L)
