@@ -302,3 +302,13 @@ def test_tc_plan_matches_list_schedule_model(tc):
         _native.check(_native.lib.lara_decode_plan(len(lens), 64, 8, 128, L, lens.ctypes.data, ctypes.byref(ns),
                                                     ctypes.byref(ch)), "plan")
         assert (ns.value, ch.value) == _list_schedule_plan(lens.tolist(), L, 8, sms), (len(lens), L)
+
+
+@pytest.mark.slow
+def test_tc_long_sequence_many_splits(tc):
+    """One 300,000-token sequence at G = 8 (the planner's split count, and a
+    forced 300-way split whose merge spans more than 32 splits per pass)."""
+    B, Hq, Hkv, L = 1, 64, 8, 300_000
+    for splits in ((0, 0), (300, 1024)):
+        o, gold, g64, dec = _case(tc, B, Hq, Hkv, [L], L, seed=31, std=0.5, splits=splits)
+        assert_bf16_parity(o, gold, g64, what=f"tc long sequence splits={splits} plan={dec.plan}")
