@@ -663,10 +663,47 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     torch.cuda.synchronize(dev)
     k_ms = ka.elapsed_time(kb) / max(3, args.steps // 4)
     clocks = sampler.summary()
+    o_kernel = o.clone()
+
+    # e2e: the public torch API with pinned host buffers -- the chunk's q and
+    # new K/V go host->device, the output comes back, every step
+    e2e_ms, h2d, d2h = None, 0, 0
+    if not args.no_e2e:
+        qh, knh, vnh = (t.cpu().pin_memory() for t in (q, kn, vn))
+        oh = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        qd, knd, vnd = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+
+        def e2e_step():
+            qd.copy_(qh, non_blocking=True)
+            knd.copy_(knh, non_blocking=True)
+            vnd.copy_(vnh, non_blocking=True)
+            lens.copy_(lens0)
+            ops.kv_append(k, v, lens, knd, vnd, workspace=ws)
+            ops.gqa_prefill(qd, k, v, lens0, causal=True, workspace=ws, out=o)
+            oh.copy_(o, non_blocking=True)
+            stream.synchronize()
+
+        for _ in range(2):
+            e2e_step()
+        n_e2e = max(3, min(args.steps, 20))
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            e2e_step()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
+        if not torch.equal(oh.view(torch.int16), o_kernel.cpu().view(torch.int16)):
+            raise RuntimeError("API output differs from the timed kernel output")
+        h2d = qh.numel() * 2 + knh.numel() * 2 + vnh.numel() * 2
+        d2h = oh.numel() * 2
     if world > 1:
-        t = torch.tensor([ms, k_ms], dtype=torch.float64, device=dev)
+        t = torch.tensor([ms, k_ms, e2e_ms or 0.0], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, k_ms = float(t[0]), float(t[1])
+        e2e_ms = float(t[2]) if e2e_ms is not None else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = prefill_cpu_baseline(cfg, q, k, v, args.cpu_seconds)
     if rank != 0:
         return 0
     flops = cfg.flops()
@@ -692,10 +729,63 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_flop_per_launch": flops, "attention_kernel_ms": round(k_ms, 4)},
+        "cpu_baseline": cpu,
+        "e2e": None if e2e_ms is None else {
+            "value": round(flops * world / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+            "api": "ops.kv_append + ops.gqa_prefill (pinned host q, k_new, v_new, o)"},
         "gpu_launches": args.steps * 3, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def prefill_cpu_baseline(cfg, q, k, v, seconds: float) -> dict:
+    """The CPU oracle's chunked prefill (oracle.prefill_attention, the causal rule of
+    sw/board_performance.py:174-177 over cache + self) for the kv-head groups of
+    sequence 0, timed per pass on all host cores and on one thread."""
+    import concurrent.futures as cf
+
+    import torch
+
+    import oracle
+
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    B, n, Hq, D = q.shape
+    Hkv, C = cfg.n_kv_heads, cfg.cached
+    G = Hq // Hkv
+    words = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    qw = words(q[0]).transpose(1, 0, 2)[None]          # [1, Hq, n, D]
+    kw, vw = words(k[0])[None], words(v[0])[None]      # [1, Hkv, Lmax, D], chunk already appended
+    kv_len = np.array([C + n])
+    flop_group = G * (n * C + n * (n + 1) // 2) * 4 * D
+
+    def unit(g):
+        oracle.prefill_attention(qw[:, g * G:(g + 1) * G], kw[:, g:g + 1], vw[:, g:g + 1], kv_len, C, causal=True)
+
+    def passes(threads, groups, repeats, min_s):
+        times = []
+        with cf.ThreadPoolExecutor(max_workers=threads) as pool:
+            list(pool.map(unit, groups))  # warm-up
+            t_start = time.perf_counter()
+            while len(times) < repeats or time.perf_counter() - t_start < min_s:
+                t0 = time.perf_counter_ns()
+                list(pool.map(unit, groups))
+                times.append((time.perf_counter_ns() - t0) * 1e-9)
+        return times
+
+    groups = list(range(Hkv))
+    t_all = passes(min(cores, Hkv), groups, 3, seconds)
+    st_all = pass_stats(t_all)
+    t_one = passes(1, groups[:1], 3, 0.0)
+    st_one = pass_stats(t_one)
+    return {"value": round(flop_group * len(groups) / st_all["median_s"] / 1e12, 5), "unit": "TFLOP/s",
+            "cores": min(cores, Hkv), "kind": "port",
+            "sample": f"the {Hkv} kv-head groups of sequence 0 ({G} query heads each, {n} queries over {C} cached "
+                      f"+ self), one group per thread; value from the median pass",
+            "pass_seconds": st_all,
+            "single_thread": {"value": round(flop_group / st_one["median_s"] / 1e12, 5), "unit": "TFLOP/s",
+                              "cores": 1, "sample": "kv-head group 0 of sequence 0", "pass_seconds": st_one}}
 
 
 def run_prologue(args, rank: int, world: int, local_rank: int) -> int:

@@ -177,6 +177,35 @@ def kv_append(k_cache, v_cache, seq_lens, k_new, v_new, workspace=None) -> None:
           "lara_kv_append")
 
 
+def gqa_prefill(q, k_cache, v_cache, cached_lens, *, causal=True, scale=None, workspace=None, out=None):
+    """Chunked prefill over the cache ("cache + self").
+
+    ``q[B, n, Hq, D]`` (token-major) attends the cache ``k/v_cache[B, Hkv, Lmax, D]``
+    whose rows ``cached_lens[b] .. cached_lens[b] + n - 1`` already hold the chunk's
+    own K/V (``kv_append`` with the lengths before the append); query ``i`` of
+    sequence ``b`` sits at position ``cached_lens[b] + i`` and, when ``causal``,
+    sees keys ``0 .. cached_lens[b] + i``.  Returns ``o[B, n, Hq, D]`` (bf16).
+    """
+    B, n, Hq, D = q.shape
+    _, Hkv, Lmax, _ = k_cache.shape
+    _check_words("q", q)
+    _check_words("k_cache", k_cache, (B, Hkv, Lmax, D))
+    _check_words("v_cache", v_cache, (B, Hkv, Lmax, D))
+    if cached_lens.dtype != torch.int32 or not cached_lens.is_cuda or cached_lens.numel() != B:
+        raise ValueError("cached_lens must be a CUDA int32 tensor of length batch")
+    nbytes = int(lib.lara_prefill_workspace_bytes(B, n, Hq, Hkv, D, Lmax))
+    if nbytes == 0:
+        raise ValueError(f"unsupported prefill geometry B={B} n={n} Hq={Hq} Hkv={Hkv} D={D} Lmax={Lmax}")
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = new_workspace(nbytes, q.device)
+    o = torch.empty_like(q) if out is None else out
+    sc = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    check(lib.lara_gqa_prefill(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), cached_lens.data_ptr(),
+                               o.data_ptr(), B, n, Hq, Hkv, D, Lmax, int(bool(causal)), sc, workspace.data_ptr(),
+                               workspace.numel(), _stream(q.device)), "lara_gqa_prefill")
+    return o
+
+
 def pack_bf16(x: torch.Tensor) -> torch.Tensor:
     """fp32 -> bf16 words (int16 view), bit-identical to the reference packer."""
     if x.dtype != torch.float32 or not x.is_cuda:

@@ -153,3 +153,25 @@ def test_config5_full_size_sampled(monkeypatch):
             qs = qw[b:b + 1, i0:i0 + 16].transpose(0, 2, 1, 3)
             gold = oracle.prefill_attention(qs, kw, vw, np.array([C + n]), C + i0, causal=True)[0]
             assert_bf16_parity(o[b, i0:i0 + 16].transpose(1, 0, 2), gold, what=f"cfg5 b={b} rows {i0}+16")
+
+
+def test_ops_gqa_prefill_matches_abi():
+    """The torch front end ``ops.gqa_prefill`` returns the C ABI's words."""
+    from lara_b200 import ops
+
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    B, Hq, Hkv, D, cached, n = 2, 32, 8, 128, [300, 17], 150
+    Lmax = max(cached) + n + 3
+    q = (torch.randn((B, n, Hq, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    k = (torch.randn((B, Hkv, Lmax, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((B, Hkv, Lmax, D), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    lens = torch.tensor(cached, dtype=torch.int32, device=dev)
+    o_abi = words_of(_prefill(dev, q, k, v, cached, True))
+    o_ops = words_of(ops.gqa_prefill(q, k, v, lens, causal=True))
+    np.testing.assert_array_equal(o_ops, o_abi)
+    with pytest.raises(ValueError):
+        ops.gqa_prefill(q, k, v, lens.to(torch.int64))
