@@ -851,10 +851,46 @@ def run_prologue(args, rank: int, world: int, local_rank: int) -> int:
     barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
     clocks = sampler.summary()
+    outs_kernel = [t.clone() for t in (q, k, v)]
+
+    # e2e: ops.layer_prologue with the hidden states from pinned host memory and
+    # q/k/v read back every step (weights resident)
+    e2e_ms, h2d, d2h = None, 0, 0
+    if not args.no_e2e:
+        xh = x.cpu().pin_memory()
+        hosts = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (q, k, v)]
+        xd = torch.empty_like(x)
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            ops.layer_prologue(xd, w, rms, n_q_heads=hq, n_kv_heads=hkv, head_dim=D, q_pos_base=base_pos,
+                               kv_pos_base=base_pos, workspace=wss[0], out=(q, k, v))
+            for hb, t in zip(hosts, (q, k, v)):
+                hb.copy_(t, non_blocking=True)
+            stream.synchronize()
+
+        for _ in range(2):
+            e2e_step()
+        n_e2e = max(3, min(args.steps, 20))
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            e2e_step()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
+        for hb, t in zip(hosts, outs_kernel):
+            if not torch.equal(hb.view(torch.int16), t.cpu().view(torch.int16)):
+                raise RuntimeError("API output differs from the timed kernel output")
+        h2d = xh.numel() * 2
+        d2h = sum(hb.numel() * 2 for hb in hosts)
     if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        t = torch.tensor([ms, e2e_ms or 0.0], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
+        e2e_ms = float(t[1]) if e2e_ms is not None else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = prologue_cpu_baseline(x, w, rms, hq, hkv, D, base_pos, args.cpu_seconds)
     if rank != 0:
         return 0
     flops = 2.0 * B * L * hidden * n_total
@@ -879,10 +915,58 @@ def run_prologue(args, rank: int, world: int, local_rank: int) -> int:
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
                      "algorithmic_flop_per_step": flops,
                      "note": "step time includes the RMSNorm and RoPE-table kernels (3 launches per step)"},
+        "cpu_baseline": cpu,
+        "e2e": None if e2e_ms is None else {
+            "value": round(flops * world / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+            "api": "ops.layer_prologue (pinned host x in, q/k/v out)"},
         "gpu_launches": args.steps * 3, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def prologue_cpu_baseline(x, w, rms, hq, hkv, D, base_pos, seconds: float) -> dict:
+    """The CPU oracle's layer prologue (oracle.prologue.layer_prologue: RMSNorm, fp64
+    projection, RoPE) on 8 blocks of 32 tokens of sequence 0, one block per thread."""
+    import concurrent.futures as cf
+
+    import torch
+
+    from oracle import prologue as oracle_prologue
+
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    words = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    blocks, tok = 8, 32
+    xw = words(x[0, :blocks * tok])
+    ww, rw = words(w), words(rms)
+    hidden, n_total = ww.shape
+    flop_block = 2.0 * tok * hidden * n_total
+
+    def unit(i):
+        oracle_prologue.layer_prologue(xw[i * tok:(i + 1) * tok], ww, rw, n_q_heads=hq, n_kv_heads=hkv,
+                                       head_dim=D, q_pos_base=base_pos + i * tok, kv_pos_base=base_pos + i * tok)
+
+    def passes(threads, ids, repeats, min_s):
+        times = []
+        with cf.ThreadPoolExecutor(max_workers=threads) as pool:
+            list(pool.map(unit, ids))
+            t_start = time.perf_counter()
+            while len(times) < repeats or time.perf_counter() - t_start < min_s:
+                t0 = time.perf_counter_ns()
+                list(pool.map(unit, ids))
+                times.append((time.perf_counter_ns() - t0) * 1e-9)
+        return times
+
+    threads = min(cores, blocks)
+    st_all = pass_stats(passes(threads, list(range(blocks)), 3, seconds))
+    st_one = pass_stats(passes(1, [0], 3, 0.0))
+    return {"value": round(flop_block * blocks / st_all["median_s"] / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{blocks} blocks of {tok} tokens of sequence 0, one block per thread; value from the median pass",
+            "pass_seconds": st_all,
+            "single_thread": {"value": round(flop_block / st_one["median_s"] / 1e12, 5), "unit": "TFLOP/s",
+                              "cores": 1, "sample": f"one block of {tok} tokens", "pass_seconds": st_one}}
 
 
 def main() -> int:

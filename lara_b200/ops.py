@@ -251,11 +251,13 @@ def attention_dense_board(q, k, v, *, causal=True, q_pos_base=0, kv_pos_base=0):
 
 
 def layer_prologue(x, w_qkv, rms_weight=None, *, n_q_heads=32, n_kv_heads=8, head_dim=128, q_pos_base=0,
-                   kv_pos_base=0, rms_eps=1e-5, rope_base=10000.0):
+                   kv_pos_base=0, rms_eps=1e-5, rope_base=10000.0, workspace=None, out=None):
     """RMSNorm -> QKV projection -> RoPE on device tensors (``lara_layer_prologue``).
 
     x: bf16 [L, hidden] or [B, L, hidden]; w_qkv: bf16 [hidden, (Hq + 2 Hkv) * D] (= [Wq | Wk | Wv]);
-    rms_weight: bf16 [hidden] or None.  Returns bf16 q [(B,) Hq, L, D], k [(B,) Hkv, L, D], v likewise.
+    rms_weight: bf16 [hidden] or None.  Returns bf16 q [(B,) Hq, L, D], k [(B,) Hkv, L, D], v likewise
+    (into ``out = (q, k, v)`` when given).  ``workspace`` (from ``new_workspace``) is reused when large
+    enough.
     """
     batched = x.dim() == 3
     B, L, hidden = x.shape if batched else (1, *x.shape)
@@ -266,11 +268,17 @@ def layer_prologue(x, w_qkv, rms_weight=None, *, n_q_heads=32, n_kv_heads=8, hea
         _check_words("rms_weight", rms_weight, (hidden,))
     dev = x.device
     lead = (B,) if batched else ()
-    q = torch.empty((*lead, n_q_heads, L, head_dim), dtype=x.dtype, device=dev)
-    k = torch.empty((*lead, n_kv_heads, L, head_dim), dtype=x.dtype, device=dev)
-    v = torch.empty_like(k)
+    if out is None:
+        q = torch.empty((*lead, n_q_heads, L, head_dim), dtype=x.dtype, device=dev)
+        k = torch.empty((*lead, n_kv_heads, L, head_dim), dtype=x.dtype, device=dev)
+        v = torch.empty_like(k)
+    else:
+        q, k, v = out
+        _check_words("q", q, (*lead, n_q_heads, L, head_dim))
+        _check_words("k", k, (*lead, n_kv_heads, L, head_dim))
+        _check_words("v", v, (*lead, n_kv_heads, L, head_dim))
     nbytes = int(lib.lara_layer_prologue_workspace_bytes(B, L, hidden))
-    ws = new_workspace(nbytes, dev)
+    ws = workspace if workspace is not None and workspace.numel() >= nbytes else new_workspace(nbytes, dev)
     check(lib.lara_layer_prologue(x.data_ptr(), 0 if rms_weight is None else rms_weight.data_ptr(), w_qkv.data_ptr(),
                                   q.data_ptr(), k.data_ptr(), v.data_ptr(), B, L, hidden, n_q_heads, n_kv_heads,
                                   head_dim, q_pos_base, kv_pos_base, float(rms_eps), float(rope_base),
