@@ -210,7 +210,10 @@ __device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, volat
   return __all_sync(kFull, ok);
 }
 
-template <int G>
+// kPaged: K/V in a page pool addressed through the block table; each cache
+// layout gets its own instantiation, so a kernel holds only the copy code it
+// runs (the per-tile loops are sensitive to instruction-cache pressure).
+template <int G, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     gqa_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const DecodeParams p, const TcDecodeArgs a) {
@@ -287,33 +290,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int st = n % kStages;
       if (n >= kStages && !wait_or_abort(&bars->empty[st], ((n / kStages) - 1) & 1, abort)) return false;
       metas[st] = m;
-      if (copies && a.page_box == 0) {
-        uint8_t* ks = smem + kKOff + st * kKVBytes;
-        uint8_t* vs = smem + kVOff + st * kKVBytes;
-        mbar_arrive_expect_tx(&bars->full[st], 2 * kKVBytes);
-        tma_load_4d_hint(ks, &tm_k, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
-        tma_load_4d_hint(ks + kHalf, &tm_k, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
-        tma_load_4d_hint(vs, &tm_v, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
-        tma_load_4d_hint(vs + kHalf, &tm_v, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
-      } else if (copies) {
-        // paged cache: the tile is page_box-row pieces of whole pages (tiles
-        // start on 128-token boundaries); pieces past the item's end are not
-        // loaded (their rows are masked, and V rows zeroed, by the softmax)
-        uint8_t* ks = smem + kKOff + st * kKVBytes;
-        uint8_t* vs = smem + kVOff + st * kKVBytes;
-        const int bx = a.page_box;
-        const int pieces = min(kTile / bx, (m.tok_end - m.tok0 + bx - 1) / bx);
-        mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
-        const int ps_mask = (1 << p.page_log2) - 1;
-        for (int i = 0; i < pieces; ++i) {
-          const int tok = m.tok0 + i * bx;
-          const int pg = page_at(tok);
-          const int in_page = tok & ps_mask;
-          const int off = i * bx * 128;
-          tma_load_4d_hint(ks + off, &tm_k, 0, in_page, m.kvh, pg, &bars->full[st], pol);
-          tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, in_page, m.kvh, pg, &bars->full[st], pol);
-          tma_load_4d_hint(vs + off, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
-          tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+      if (copies) {
+        if constexpr (!kPaged) {
+          uint8_t* ks = smem + kKOff + st * kKVBytes;
+          uint8_t* vs = smem + kVOff + st * kKVBytes;
+          mbar_arrive_expect_tx(&bars->full[st], 2 * kKVBytes);
+          tma_load_4d_hint(ks, &tm_k, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+          tma_load_4d_hint(ks + kHalf, &tm_k, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+          tma_load_4d_hint(vs, &tm_v, 0, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+          tma_load_4d_hint(vs + kHalf, &tm_v, 64, m.tok0, m.kvh, m.seq_kv, &bars->full[st], pol);
+        } else {
+          // paged cache: the tile is page_box-row pieces of whole pages (tiles
+          // start on 128-token boundaries); pieces past the item's end are not
+          // loaded (their rows are masked, and V rows zeroed, by the softmax)
+          uint8_t* ks = smem + kKOff + st * kKVBytes;
+          uint8_t* vs = smem + kVOff + st * kKVBytes;
+          const int bx = a.page_box;
+          const int pieces = min(kTile / bx, (m.tok_end - m.tok0 + bx - 1) / bx);
+          mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
+          const int ps_mask = (1 << p.page_log2) - 1;
+          for (int i = 0; i < pieces; ++i) {
+            const int tok = m.tok0 + i * bx;
+            const int pg = page_at(tok);
+            const int in_page = tok & ps_mask;
+            const int off = i * bx * 128;
+            tma_load_4d_hint(ks + off, &tm_k, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+            tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+            tma_load_4d_hint(vs + off, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+            tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+          }
         }
       } else {
         mbar_arrive(&bars->full[st]);
@@ -367,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       m.tok_end = tok_begin + ntok;
       m.nsplit_b = len <= c0 ? 1 : 1 + (len - c0 + p.chunk - 1) / p.chunk;
       m.seq_kv = a.kv_shared ? 0 : seq;
-      if (a.page_box) {
+      if constexpr (kPaged) {
         bt_row = p.block_table + (long long)seq * p.pages_per_seq;
         pg0 = tok_begin >> p.page_log2;
         const int np = min(kPageCache, ((m.tok_end - 1) >> p.page_log2) - pg0 + 1);
@@ -709,15 +714,20 @@ DecodePath path_override() {
 // the CUDA-core kernel streams K/V at the HBM rate already.
 constexpr int kAutoMinGroup = 8;
 
-const void* kernel_for(int group) {
+template <bool kPaged>
+const void* kernel_for_layout(int group) {
   switch (group) {
-    case 1: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<1>);
-    case 2: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<2>);
-    case 4: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<4>);
-    case 8: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<8>);
-    case 16: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<16>);
+    case 1: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<1, kPaged>);
+    case 2: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<2, kPaged>);
+    case 4: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<4, kPaged>);
+    case 8: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<8, kPaged>);
+    case 16: return reinterpret_cast<const void*>(&gqa_decode_tc_kernel<16, kPaged>);
     default: return nullptr;
   }
+}
+
+const void* kernel_for(int group, bool paged = false) {
+  return paged ? kernel_for_layout<true>(group) : kernel_for_layout<false>(group);
 }
 
 bool stride_ok(long long elems) { return elems > 0 && (elems * 2) % 16 == 0 && elems * 2 < (1ll << 40); }
@@ -787,9 +797,9 @@ void decode_tc_plan(int batch, int n_kv_heads, int max_tokens, const int32_t* le
 
 cudaError_t decode_tc_launch(const DecodeParams& p, cudaStream_t stream) {
   const int group = p.n_kv_heads > 0 ? p.n_q_heads / p.n_kv_heads : 0;
-  const void* fn = kernel_for(group);
-  if (!fn || p.head_dim != kD) return cudaErrorNotSupported;
   const bool paged = p.block_table != nullptr;
+  const void* fn = kernel_for(group, paged);
+  if (!fn || p.head_dim != kD) return cudaErrorNotSupported;
   auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
   if (!al16(p.q) || !al16(p.k) || !al16(p.v) || !stride_ok(p.q_sh)) return cudaErrorNotSupported;
   if (p.batch > 1 && !stride_ok(p.q_sb)) return cudaErrorNotSupported;
