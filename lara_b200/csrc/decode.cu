@@ -116,7 +116,7 @@ __device__ __forceinline__ int page_of(const DecodeParams& p, const int* pcache,
 }
 
 // Issue the bulk copies of tile `t` (K rows then V rows) into stage `st`.
-template <int D, int G>
+template <int D, int G, bool kPaged>
 __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t, int ntok, const DecodeParams& p,
                                            int seq, int kvh, int tok_begin, const int* pcache, uint64_t pol) {
   using T = Traits<D, G>;
@@ -126,7 +126,7 @@ __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t,
   uint8_t* stage = smem + st * T::kStageBytes;
   mbar_arrive_expect_tx(&full[st], 2u * bytes);
   const int tok0 = tok_begin + t * T::kTile;
-  if (p.block_table == nullptr) {
+  if constexpr (!kPaged) {
     const long long off = (long long)seq * p.kv_sb + (long long)kvh * p.kv_sh + (long long)tok0 * D;
     bulk_g2s(stage, p.k + off, bytes, &full[st], pol);
     bulk_g2s(stage + T::kHalfStage, p.v + off, bytes, &full[st], pol);
@@ -145,7 +145,9 @@ __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t,
   }
 }
 
-template <int D, int G>
+// kPaged: K/V in a page pool addressed through the block table; each cache
+// layout gets its own instantiation, so a kernel holds only the copy code it runs.
+template <int D, int G, bool kPaged>
 __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBlocks)
     gqa_decode_kernel(const DecodeParams p) {
   using T = Traits<D, G>;
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
 
   const uint64_t pol = make_evict_first_policy();
   int* pcache = reinterpret_cast<int*>(smem + T::kPageOff);
-  if (p.block_table != nullptr) {
+  if constexpr (kPaged) {
     // block-table entries of this CTA's chunk (the first kPageCache of them)
     const int first_page = tok_begin >> p.page_log2;
     const int npages = min(T::kPageCache, ((tok_begin + ntok - 1) >> p.page_log2) - first_page + 1);
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     flag[2] = 0;  // tiles issued
     mbar_fence_init();
     const int first = ntiles < T::kStages ? ntiles : T::kStages;
-    for (int t = 0; t < first; ++t) issue_tile<D, G>(smem, full, t, ntok, p, seq, kvh, tok_begin, pcache, pol);
+    for (int t = 0; t < first; ++t) issue_tile<D, G, kPaged>(smem, full, t, ntok, p, seq, kvh, tok_begin, pcache, pol);
     flag[2] = first;
   }
   __syncthreads();
@@ -379,7 +381,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
       const int nxt = i + T::kStages;
       if (nxt < ntiles && mbar_test_wait(&empty[st], round & 1) &&
           atomicCAS(&refill_round[st], round, round + 1) == round) {
-        issue_tile<D, G>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pcache, pol);
+        issue_tile<D, G, kPaged>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pcache, pol);
         atomicMax(&flag[2], nxt + 1);
       }
     }
@@ -489,14 +491,16 @@ struct KernelInfo {
 };
 
 template <int D, int G>
-KernelInfo info_for() {
+KernelInfo info_for(bool paged) {
   using T = Traits<D, G>;
-  return KernelInfo{reinterpret_cast<const void*>(&gqa_decode_kernel<D, G>), T::kThreads, T::kSmemBytes, T::kTile};
+  const void* fn = paged ? reinterpret_cast<const void*>(&gqa_decode_kernel<D, G, true>)
+                         : reinterpret_cast<const void*>(&gqa_decode_kernel<D, G, false>);
+  return KernelInfo{fn, T::kThreads, T::kSmemBytes, T::kTile};
 }
 
-KernelInfo lookup(int D, int G) {
+KernelInfo lookup(int D, int G, bool paged = false) {
 #define LARA_CASE(d, g) \
-  if (D == d && G == g) return info_for<d, g>();
+  if (D == d && G == g) return info_for<d, g>(paged);
   LARA_CASE(128, 1) LARA_CASE(128, 2) LARA_CASE(128, 4) LARA_CASE(128, 8)
   LARA_CASE(64, 1) LARA_CASE(64, 2) LARA_CASE(64, 4) LARA_CASE(64, 8)
 #undef LARA_CASE
@@ -625,7 +629,7 @@ cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream) {
     const cudaError_t e = decode_tc_launch(p, stream);
     if (e != cudaErrorNotSupported) return e;
   }
-  const KernelInfo k = lookup(p.head_dim, group);
+  const KernelInfo k = lookup(p.head_dim, group, p.block_table != nullptr);
   if (!k.fn) return cudaErrorInvalidValue;
   if (p.chunk <= 0 || p.chunk % k.tile != 0 || p.nsplit <= 0) return cudaErrorInvalidValue;
   if (p.chunk0 < 0 || p.chunk0 % k.tile != 0) return cudaErrorInvalidValue;
