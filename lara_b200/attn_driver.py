@@ -378,6 +378,19 @@ class AttentionAccelerator:
     def last_profile(self) -> RunProfile | None:
         # run_query finishes its profile only when it is read (the device times
         # come from CUDA events; reading them is work a decode loop need not pay)
+        query = self.__dict__.get("_pending_query")
+        if query is not None:
+            self._pending_query = None
+            ts, t_start, t_call, t_end, q_bytes, o_bytes, seq_len = query
+            prof = RunProfile(timestamp_utc=datetime.fromtimestamp(ts, timezone.utc).isoformat(),
+                              git_commit=self._git_hash, bitstream_sha256=self._bitstream_hash,
+                              clock_mhz=self._pl_clock_mhz, seq_len=seq_len, causal=False, q_pos_base=0,
+                              kv_pos_base=0)
+            prof.request_service_ms = (t_end - t_call) * 1000.0
+            prof.q_dma_transfers, prof.q_dma_bytes = 1, q_bytes
+            prof.output_dma_transfers, prof.output_dma_bytes = 1, o_bytes
+            self._last_profile = prof
+            self._pending_profile = (prof, t_start, t_end)
         pending = self.__dict__.get("_pending_profile")
         if pending is not None:
             self._pending_profile = None
@@ -386,6 +399,7 @@ class AttentionAccelerator:
 
     @last_profile.setter
     def last_profile(self, prof: RunProfile | None) -> None:
+        self._pending_query = None
         self._pending_profile = None
         self._last_profile = prof
 
@@ -582,22 +596,31 @@ class AttentionAccelerator:
         self._require_open()
         t_start = time.perf_counter()
         shape = (self.batch, self.n_q_heads, self.head_dim)
-        qw = _words("Q", q, shape)
+        if type(q) is np.ndarray and q.dtype == np.uint16 and q.shape == shape and q.flags.c_contiguous:
+            qw = q  # the decode-loop case: already contiguous bf16 words
+        else:
+            qw = _words("Q", q, shape)
         if out is None:
             out = np.empty(shape, dtype=np.uint16)
         elif out.shape != shape or out.dtype != np.uint16 or not out.flags.c_contiguous:
             raise ValueError(f"out must be a contiguous uint16 array of shape {shape}")
-        prof = self._new_profile(self._max_len, False, 0, 0)
-        self.last_profile = prof
+        # data addresses of the last q / out arrays, held with the arrays themselves
+        # (a decode loop passes the same buffers every step)
+        cache = self.__dict__.get("_query_ptrs")
+        if cache is None or cache[0] is not qw or cache[2] is not out:
+            cache = self._query_ptrs = (qw, qw.ctypes.data, out, out.ctypes.data)
         self._status_word = STATUS_BUSY
         t = time.perf_counter()
-        check(lib.lara_run_query(self._ctx, _ptr(qw), _ptr(out), 0), "run_query")
-        prof.request_service_ms = (time.perf_counter() - t) * 1000.0
+        rc = lib.lara_run_query(self._ctx, cache[1], cache[3], 0)
+        if rc:
+            check(rc, "run_query")
+        t_end = time.perf_counter()
         self._status_word = STATUS_DONE | STATUS_START_READY
-        prof.q_dma_transfers, prof.q_dma_bytes = 1, qw.nbytes
-        prof.output_dma_transfers, prof.output_dma_bytes = 1, out.nbytes
         self._last_output = out
-        self._pending_profile = (prof, t_start, time.perf_counter())
+        # The RunProfile is built when last_profile is read: a decode loop pays
+        # for two clock reads, not for the record.
+        self._pending_profile = None
+        self._pending_query = (time.time(), t_start, t, t_end, qw.nbytes, out.nbytes, self._max_len)
         return out
 
     def run_prefill_chunk(self, q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, *,

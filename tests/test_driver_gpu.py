@@ -299,3 +299,30 @@ def test_async_decode_and_prefill_match_synchronous_calls():
         _native.check(lib.lara_sync(async_acc._ctx, 10_000), "lara_sync")
         np.testing.assert_array_equal(words_of(op), want_p)
         assert async_acc.seq_lens.tolist() == (lens + n).tolist()
+
+
+def test_run_query_profile_is_built_on_read():
+    """run_query records two clock reads; last_profile builds the RunProfile (with
+    the device times of the call) on its first read and describes the query,
+    not the cache as it is when the profile is read."""
+    from lara_b200.attn_driver import AttentionAccelerator
+
+    rng = np.random.default_rng(4)
+    B, Hq, Hkv, D, L = 2, 32, 8, 128, 300
+    pk = oracle.fp32_to_bf16_u16
+    k = pk(rng.standard_normal((B, Hkv, L, D)).astype(np.float32))
+    v = pk(rng.standard_normal((B, Hkv, L, D)).astype(np.float32))
+    q = pk(rng.standard_normal((B, Hq, D)).astype(np.float32))
+    with AttentionAccelerator() as a:
+        a.configure_heads(Hq, Hkv, D, max_seq_len=L + 8, batch=B)
+        a.load_kv(k, v)
+        a.run_query(q)
+        prof = a.last_profile
+        assert prof is not None and prof.pl_total_cycles > 0
+        assert 0 <= prof.pl_mac_cycles <= prof.pl_total_cycles
+        assert prof.q_dma_bytes == q.nbytes and prof.output_dma_bytes == q.nbytes
+        assert prof.seq_len == L and prof.timestamp_utc and prof.attention_total_ms > 0
+        assert a.last_profile is prof
+        a.run_query(q)
+        a.append_kv(np.zeros((B, Hkv, 1, D), np.uint16), np.zeros((B, Hkv, 1, D), np.uint16))
+        assert a.last_profile.seq_len == L
