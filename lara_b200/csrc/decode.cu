@@ -84,8 +84,8 @@ struct Traits {
   static constexpr int kCntOff = kBarOff + 2 * kStages * 8;                      // refill round per stage
   static constexpr int kFlagOff = kCntOff + kStages * 4;
   static constexpr int kPageCache = kPageCacheEntries;
-  static constexpr int kPageOff = kFlagOff + 16;
-  static constexpr int kSmemBytes = kPageOff + kPageCache * 4;
+  static constexpr int kPageOff = (kFlagOff + 16 + 15) / 16 * 16;                // page offsets (int64)
+  static constexpr int kSmemBytes = kPageOff + kPageCache * 8;
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
   static_assert(kLPT <= 32 && 32 % kLPT == 0, "a token row must fit one warp");
   static_assert(G >= 1 && G <= kLPT && (G & (G - 1)) == 0, "group size must be a power of two <= lanes per row");
@@ -102,23 +102,44 @@ __device__ __forceinline__ int seq_len_of(const DecodeParams& p, int seq, int ro
   return len < 0 ? 0 : (len > p.max_seq_len ? p.max_seq_len : (int)len);
 }
 
-// Page of the token `tok` of `seq` (paged caches).  Entries of the CTA's chunk
-// are staged in shared memory; an out-of-range entry flags the status word and
-// reads page 0 instead, so every issued copy stays in bounds and completes.
-__device__ __forceinline__ int page_of(const DecodeParams& p, const int* pcache, int seq, int tok, int tok_begin) {
-  const int idx = (tok >> p.page_log2) - (tok_begin >> p.page_log2);
-  int page = idx < kPageCacheEntries ? pcache[idx] : __ldg(p.block_table + (long long)seq * p.pages_per_seq + (tok >> p.page_log2));
-  if (page < 0 || page >= p.num_pages) {
-    atomicOr(p.status, kDevBadPage);
+// Paged caches: element offset of the (page, kv head) block that holds token
+// `tok` of `seq` in the pool [pages][Hkv][page][D].  An out-of-range
+// block-table entry flags the status word and reads page 0 instead, so every
+// issued copy stays in bounds and completes.
+__device__ __forceinline__ long long page_block(const int32_t* block_table, int pages_per_seq, int page_log2,
+                                                int num_pages, int n_kv_heads, int* status, int seq, int kvh,
+                                                int tok, int d) {
+  int page = __ldg(block_table + (long long)seq * pages_per_seq + (tok >> page_log2));
+  if (page < 0 || page >= num_pages) {
+    atomicOr(status, kDevBadPage);
     page = 0;
   }
-  return page;
+  return (((long long)page * n_kv_heads + kvh) << page_log2) * d;
+}
+
+// The same, for a page past the CTA's shared-memory cache (chunks of more than
+// kPageCacheEntries pages), kept out of line so the refill path stays short.
+__device__ __noinline__ long long page_block_uncached(const int32_t* block_table, int pages_per_seq, int page_log2,
+                                                      int num_pages, int n_kv_heads, int* status, int seq, int kvh,
+                                                      int tok, int d) {
+  return page_block(block_table, pages_per_seq, page_log2, num_pages, n_kv_heads, status, seq, kvh, tok, d);
+}
+
+// Offset of the block holding `tok`: from the CTA's validated cache of the
+// chunk's pages, or from the block table past it.
+template <int D>
+__device__ __forceinline__ long long page_base(const DecodeParams& p, const long long* pbase, int seq, int kvh,
+                                               int tok, int tok_begin) {
+  const int idx = (tok >> p.page_log2) - (tok_begin >> p.page_log2);
+  if (idx < kPageCacheEntries) return pbase[idx];
+  return page_block_uncached(p.block_table, p.pages_per_seq, p.page_log2, p.num_pages, p.n_kv_heads, p.status, seq,
+                             kvh, tok, D);
 }
 
 // Issue the bulk copies of tile `t` (K rows then V rows) into stage `st`.
 template <int D, int G, bool kPaged>
 __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t, int ntok, const DecodeParams& p,
-                                           int seq, int kvh, int tok_begin, const int* pcache, uint64_t pol) {
+                                           int seq, int kvh, int tok_begin, const long long* pbase, uint64_t pol) {
   using T = Traits<D, G>;
   const int st = t % T::kStages;
   const int n = min(T::kTile, ntok - t * T::kTile);
@@ -132,13 +153,22 @@ __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t,
     bulk_g2s(stage + T::kHalfStage, p.v + off, bytes, &full[st], pol);
     return;
   }
-  // a tile may span several pages (page < tile) or lie inside one
+  // A tile lies inside one page when pages are at least a tile long (tiles
+  // start on tile boundaries): one copy each for K and V, as for a contiguous
+  // cache.  Smaller pages take one copy per page piece.
   const int ps = 1 << p.page_log2;
+  const int in_page0 = tok0 & (ps - 1);
+  if (n <= ps - in_page0) {
+    const long long off = page_base<D>(p, pbase, seq, kvh, tok0, tok_begin) + (long long)in_page0 * D;
+    bulk_g2s(stage, p.k + off, bytes, &full[st], pol);
+    bulk_g2s(stage + T::kHalfStage, p.v + off, bytes, &full[st], pol);
+    return;
+  }
   for (int r = 0; r < n;) {
     const int tok = tok0 + r;
     const int in_page = tok & (ps - 1);
     const int cnt = min(n - r, ps - in_page);
-    const long long off = (((long long)page_of(p, pcache, seq, tok, tok_begin) * p.n_kv_heads + kvh) * ps + in_page) * D;
+    const long long off = page_base<D>(p, pbase, seq, kvh, tok, tok_begin) + (long long)in_page * D;
     bulk_g2s(stage + r * T::kRowBytes, p.k + off, (uint32_t)cnt * T::kRowBytes, &full[st], pol);
     bulk_g2s(stage + T::kHalfStage + r * T::kRowBytes, p.v + off, (uint32_t)cnt * T::kRowBytes, &full[st], pol);
     r += cnt;
@@ -201,13 +231,15 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   float* cbuf = reinterpret_cast<float*>(smem + T::kCbufOff);
 
   const uint64_t pol = make_evict_first_policy();
-  int* pcache = reinterpret_cast<int*>(smem + T::kPageOff);
+  long long* pbase = reinterpret_cast<long long*>(smem + T::kPageOff);
   if constexpr (kPaged) {
-    // block-table entries of this CTA's chunk (the first kPageCache of them)
+    // validated block offsets of this CTA's chunk (the first kPageCache pages),
+    // so a refill reads one shared-memory word
     const int first_page = tok_begin >> p.page_log2;
     const int npages = min(T::kPageCache, ((tok_begin + ntok - 1) >> p.page_log2) - first_page + 1);
     for (int i = threadIdx.x; i < npages; i += T::kThreads)
-      pcache[i] = __ldg(p.block_table + (long long)seq * p.pages_per_seq + first_page + i);
+      pbase[i] = page_block(p.block_table, p.pages_per_seq, p.page_log2, p.num_pages, p.n_kv_heads, p.status, seq, kvh,
+                            (first_page + i) << p.page_log2, D);
     __syncthreads();
   }
 
@@ -222,7 +254,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     flag[2] = 0;  // tiles issued
     mbar_fence_init();
     const int first = ntiles < T::kStages ? ntiles : T::kStages;
-    for (int t = 0; t < first; ++t) issue_tile<D, G, kPaged>(smem, full, t, ntok, p, seq, kvh, tok_begin, pcache, pol);
+    for (int t = 0; t < first; ++t) issue_tile<D, G, kPaged>(smem, full, t, ntok, p, seq, kvh, tok_begin, pbase, pol);
     flag[2] = first;
   }
   __syncthreads();
@@ -381,7 +413,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
       const int nxt = i + T::kStages;
       if (nxt < ntiles && mbar_test_wait(&empty[st], round & 1) &&
           atomicCAS(&refill_round[st], round, round + 1) == round) {
-        issue_tile<D, G, kPaged>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pcache, pol);
+        issue_tile<D, G, kPaged>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pbase, pol);
         atomicMax(&flag[2], nxt + 1);
       }
     }

@@ -202,6 +202,20 @@ __device__ __forceinline__ void merge_splits_tc(const DecodeParams& p, int b, in
   }
 }
 
+// Page holding token `tok` of a sequence whose block-table row is `bt_row`,
+// for a token past the item's shared-memory cache (items of more than
+// kPageCache pages); out of line so the per-tile copy path stays short.  An
+// out-of-range entry flags the status word and reads page 0, so every copy
+// stays in bounds and completes.
+__device__ __noinline__ int page_uncached(const int32_t* bt_row, int tok, int page_log2, int num_pages, int* status) {
+  int pg = __ldg(bt_row + (tok >> page_log2));
+  if (pg < 0 || pg >= num_pages) {
+    atomicOr(status, kDevBadPage);
+    pg = 0;
+  }
+  return pg;
+}
+
 // 128-thread meeting point of the softmax warps on an mbarrier (bounded).
 __device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, volatile int* abort) {
   mbar_arrive(bar);
@@ -277,14 +291,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int32_t* bt_row = p.block_table;
     int pg0 = 0;  // page index held by cache entry 0 (current item)
     int n = 0, qi = 0;
-    auto page_at = [&](int tok) -> int {
+    auto page_at = [&](int tok) -> int {  // cache entries are validated when loaded
       const int idx = (tok >> p.page_log2) - pg0;
-      int pg = idx < kPageCache ? pcache[idx] : __ldg(bt_row + (tok >> p.page_log2));
-      if (pg < 0 || pg >= p.num_pages) {
-        atomicOr(p.status, kDevBadPage);
-        pg = 0;  // keep every copy in bounds
-      }
-      return pg;
+      return idx < kPageCache ? pcache[idx] : page_uncached(bt_row, tok, p.page_log2, p.num_pages, p.status);
     };
     auto push = [&](const Meta& m, bool copies) -> bool {  // lane 0
       const int st = n % kStages;
@@ -306,18 +315,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* ks = smem + kKOff + st * kKVBytes;
           uint8_t* vs = smem + kVOff + st * kKVBytes;
           const int bx = a.page_box;
-          const int pieces = min(kTile / bx, (m.tok_end - m.tok0 + bx - 1) / bx);
-          mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
           const int ps_mask = (1 << p.page_log2) - 1;
-          for (int i = 0; i < pieces; ++i) {
-            const int tok = m.tok0 + i * bx;
-            const int pg = page_at(tok);
-            const int in_page = tok & ps_mask;
-            const int off = i * bx * 128;
-            tma_load_4d_hint(ks + off, &tm_k, 0, in_page, m.kvh, pg, &bars->full[st], pol);
-            tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, in_page, m.kvh, pg, &bars->full[st], pol);
-            tma_load_4d_hint(vs + off, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
-            tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+          if (bx == kTile) {
+            // pages of >= 128 tokens: the tile is one piece of one page
+            const int pg = page_at(m.tok0);
+            const int in_page = m.tok0 & ps_mask;
+            mbar_arrive_expect_tx(&bars->full[st], 2 * kKVBytes);
+            tma_load_4d_hint(ks, &tm_k, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+            tma_load_4d_hint(ks + kHalf, &tm_k, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+            tma_load_4d_hint(vs, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+            tma_load_4d_hint(vs + kHalf, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+          } else {
+            const int pieces = min(kTile / bx, (m.tok_end - m.tok0 + bx - 1) / bx);
+            mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
+            for (int i = 0; i < pieces; ++i) {
+              const int tok = m.tok0 + i * bx;
+              const int pg = page_at(tok);
+              const int in_page = tok & ps_mask;
+              const int off = i * bx * 128;
+              tma_load_4d_hint(ks + off, &tm_k, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+              tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+              tma_load_4d_hint(vs + off, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+              tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+            }
           }
         }
       } else {
@@ -376,7 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         bt_row = p.block_table + (long long)seq * p.pages_per_seq;
         pg0 = tok_begin >> p.page_log2;
         const int np = min(kPageCache, ((m.tok_end - 1) >> p.page_log2) - pg0 + 1);
-        for (int i = lane; i < np; i += 32) pcache[i] = __ldg(bt_row + pg0 + i);
+        for (int i = lane; i < np; i += 32) {
+          int pg = __ldg(bt_row + pg0 + i);
+          if (pg < 0 || pg >= p.num_pages) {
+            atomicOr(p.status, kDevBadPage);
+            pg = 0;  // keep every copy in bounds
+          }
+          pcache[i] = pg;
+        }
         __syncwarp();
       }
       if (lane == 0) {
