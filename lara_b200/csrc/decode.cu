@@ -164,14 +164,18 @@ __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t,
     bulk_g2s(stage + T::kHalfStage, p.v + off, bytes, &full[st], pol);
     return;
   }
-  for (int r = 0; r < n;) {
-    const int tok = tok0 + r;
-    const int in_page = tok & (ps - 1);
-    const int cnt = min(n - r, ps - in_page);
-    const long long off = page_base<D>(p, pbase, seq, kvh, tok, tok_begin) + (long long)in_page * D;
+  // Pages shorter than a tile divide it, so the tile starts on a page boundary:
+  // piece i is the first cnt rows of cached page idx0 + i.
+  const int idx0 = (tok0 >> p.page_log2) - (tok_begin >> p.page_log2);
+  for (int i = 0, r = 0; r < n; ++i, r += ps) {
+    const int cnt = min(n - r, ps);
+    const int idx = idx0 + i;
+    const long long off = idx < kPageCacheEntries
+                              ? pbase[idx]
+                              : page_block_uncached(p.block_table, p.pages_per_seq, p.page_log2, p.num_pages,
+                                                    p.n_kv_heads, p.status, seq, kvh, tok0 + r, D);
     bulk_g2s(stage + r * T::kRowBytes, p.k + off, (uint32_t)cnt * T::kRowBytes, &full[st], pol);
     bulk_g2s(stage + T::kHalfStage + r * T::kRowBytes, p.v + off, (uint32_t)cnt * T::kRowBytes, &full[st], pol);
-    r += cnt;
   }
 }
 

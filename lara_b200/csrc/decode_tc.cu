@@ -326,17 +326,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_4d_hint(vs, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
             tma_load_4d_hint(vs + kHalf, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
           } else {
-            const int pieces = min(kTile / bx, (m.tok_end - m.tok0 + bx - 1) / bx);
+            // pages of < 128 tokens (bx = page size): the tile starts on a page
+            // boundary, so piece i is the whole of page pg0 + idx0 + i
+            const int lg = p.page_log2;
+            const int pieces = min(kTile >> lg, (m.tok_end - m.tok0 + bx - 1) >> lg);
+            const int idx0 = (m.tok0 >> lg) - pg0;
             mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
             for (int i = 0; i < pieces; ++i) {
-              const int tok = m.tok0 + i * bx;
-              const int pg = page_at(tok);
-              const int in_page = tok & ps_mask;
-              const int off = i * bx * 128;
-              tma_load_4d_hint(ks + off, &tm_k, 0, in_page, m.kvh, pg, &bars->full[st], pol);
-              tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, in_page, m.kvh, pg, &bars->full[st], pol);
-              tma_load_4d_hint(vs + off, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
-              tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+              const int idx = idx0 + i;
+              const int pg = idx < kPageCache ? pcache[idx]
+                                              : page_uncached(bt_row, m.tok0 + (i << lg), lg, p.num_pages, p.status);
+              const int off = (i << lg) * 128;
+              tma_load_4d_hint(ks + off, &tm_k, 0, 0, m.kvh, pg, &bars->full[st], pol);
+              tma_load_4d_hint(ks + kHalf + off, &tm_k, 64, 0, m.kvh, pg, &bars->full[st], pol);
+              tma_load_4d_hint(vs + off, &tm_v, 0, 0, m.kvh, pg, &bars->full[st], pol);
+              tma_load_4d_hint(vs + kHalf + off, &tm_v, 64, 0, m.kvh, pg, &bars->full[st], pol);
             }
           }
         }
