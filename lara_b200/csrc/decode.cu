@@ -139,7 +139,8 @@ __device__ __forceinline__ long long page_base(const DecodeParams& p, const long
 // Issue the bulk copies of tile `t` (K rows then V rows) into stage `st`.
 template <int D, int G, bool kPaged>
 __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t, int ntok, const DecodeParams& p,
-                                           int seq, int kvh, int tok_begin, const long long* pbase, uint64_t pol) {
+                                           int seq, int kvh, int tok_begin, const long long* pbase, uint64_t pol,
+                                           long long pre_base = -1) {
   using T = Traits<D, G>;
   const int st = t % T::kStages;
   const int n = min(T::kTile, ntok - t * T::kTile);
@@ -159,7 +160,8 @@ __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t,
   const int ps = 1 << p.page_log2;
   const int in_page0 = tok0 & (ps - 1);
   if (n <= ps - in_page0) {
-    const long long off = page_base<D>(p, pbase, seq, kvh, tok0, tok_begin) + (long long)in_page0 * D;
+    const long long base = pre_base >= 0 ? pre_base : page_base<D>(p, pbase, seq, kvh, tok0, tok_begin);
+    const long long off = base + (long long)in_page0 * D;
     bulk_g2s(stage, p.k + off, bytes, &full[st], pol);
     bulk_g2s(stage + T::kHalfStage, p.v + off, bytes, &full[st], pol);
     return;
@@ -301,6 +303,13 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   for (int i = 0; i < ntiles; ++i) {
     const int st = i % T::kStages;
     const int round = i / T::kStages;
+    // Paged cache: the block offset of the tile this warp may refill at the end
+    // of the iteration is read now, so the refill does not wait on it.
+    long long pre_base = -1;
+    if constexpr (kPaged) {
+      const int idx = ((tok_begin + (i + T::kStages) * T::kTile) >> p.page_log2) - (tok_begin >> p.page_log2);
+      if (lane == 0 && idx < kPageCacheEntries) pre_base = pbase[idx];
+    }
     if (!mbar_wait_bounded(&full[st], round & 1)) {
       ok = false;
       break;
@@ -417,7 +426,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
       const int nxt = i + T::kStages;
       if (nxt < ntiles && mbar_test_wait(&empty[st], round & 1) &&
           atomicCAS(&refill_round[st], round, round + 1) == round) {
-        issue_tile<D, G, kPaged>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pbase, pol);
+        issue_tile<D, G, kPaged>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pbase, pol, pre_base);
         atomicMax(&flag[2], nxt + 1);
       }
     }
