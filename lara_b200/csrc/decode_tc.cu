@@ -400,13 +400,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         bt_row = p.block_table + (long long)seq * p.pages_per_seq;
         pg0 = tok_begin >> p.page_log2;
         const int np = min(kPageCache, ((m.tok_end - 1) >> p.page_log2) - pg0 + 1);
-        for (int i = lane; i < np; i += 32) {
-          int pg = __ldg(bt_row + pg0 + i);
-          if (pg < 0 || pg >= p.num_pages) {
-            atomicOr(p.status, kDevBadPage);
-            pg = 0;  // keep every copy in bounds
+        // four entries per lane in flight at a time, then checked and stored
+        for (int i0 = 0; i0 < np; i0 += 128) {
+          int v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = i0 + 32 * u + lane;
+            v[u] = i < np ? __ldg(bt_row + pg0 + i) : 0;
           }
-          pcache[i] = pg;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = i0 + 32 * u + lane;
+            if (i < np) {
+              int pg = v[u];
+              if (pg < 0 || pg >= p.num_pages) {
+                atomicOr(p.status, kDevBadPage);
+                pg = 0;  // keep every copy in bounds
+              }
+              pcache[i] = pg;
+            }
+          }
         }
         __syncwarp();
       }
