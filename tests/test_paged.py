@@ -190,6 +190,76 @@ def test_bad_page_is_reported_not_dereferenced():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("path", ["tc", "simt"])
+def test_paged_chunk_past_the_page_cache(monkeypatch, path):
+    """One split over 9000 tokens in 16-token pages: 563 pages per chunk, past the
+    kernels' shared-memory caches of block-table entries (256 on CUDA cores, 512 on
+    the tensor-core kernel), so the later tiles read the table through the
+    out-of-cache path.  Same words as the contiguous decode with the same split,
+    within the oracle's tolerance; then a bad entry past the cache is reported."""
+    torch = _torch()
+    from lara_b200 import _native
+    from lara_b200.ops import _stream, new_workspace, workspace_status
+    from parity import assert_bf16_parity, words_of
+
+    monkeypatch.setenv("LARA_DECODE_PATH", path)
+    lib = _native.lib
+    dev = torch.device("cuda:0")
+    hkv, G, D, ps = 2, 8, 128, 16
+    hq = hkv * G
+    lens = [9000, 8200]
+    cap = 9216  # 72 tiles of 128 tokens: one split covers every sequence
+    pps = cap // ps
+    rng = np.random.default_rng(21)
+    pk = oracle.fp32_to_bf16_u16
+    B = len(lens)
+    k = pk(rng.standard_normal((B, hkv, cap, D)).astype(np.float32) * 0.5)
+    v = pk(rng.standard_normal((B, hkv, cap, D)).astype(np.float32) * 0.5)
+    q = pk(rng.standard_normal((B, hq, D)).astype(np.float32) * 0.5)
+    npg = [(n + ps - 1) // ps for n in lens]
+    total = sum(npg)
+    perm = rng.permutation(total)
+    table = np.full((B, pps), -1, np.int32)
+    kp = np.zeros((total, hkv, ps, D), np.uint16)
+    vp = np.zeros_like(kp)
+    base = 0
+    for b, n in enumerate(npg):
+        pages = perm[base:base + n]
+        table[b, :n] = pages
+        kp[pages] = k[b, :, :n * ps].reshape(hkv, n, ps, D).transpose(1, 0, 2, 3)
+        vp[pages] = v[b, :, :n * ps].reshape(hkv, n, ps, D).transpose(1, 0, 2, 3)
+        base += n
+    qt, kt, vt = _bf16(torch, q, dev), _bf16(torch, kp, dev), _bf16(torch, vp, dev)
+    tt = torch.from_numpy(table).to(dev)
+    lt = torch.tensor(lens, dtype=torch.int32, device=dev)
+    nbytes = int(lib.lara_decode_workspace_bytes(B, hq, hkv, D, 1))
+    ws = new_workspace(nbytes, dev)
+    st = _stream(dev)
+
+    def paged():
+        o = torch.empty_like(qt)
+        rc = lib.lara_gqa_decode_paged(qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), tt.data_ptr(), lt.data_ptr(),
+                                       o.data_ptr(), B, hq, hkv, D, ps, pps, total, 1.0 / np.sqrt(D), 1, cap,
+                                       ws.data_ptr(), ws.numel(), st)
+        assert rc == 0, _native.last_error()
+        return o
+
+    o_paged = words_of(paged())
+    assert workspace_status(ws) == 0
+    kc, vc = _bf16(torch, k, dev), _bf16(torch, v, dev)
+    oc = torch.empty_like(qt)
+    rc = lib.lara_gqa_decode(qt.data_ptr(), kc.data_ptr(), vc.data_ptr(), lt.data_ptr(), oc.data_ptr(), B, hq, hkv, D,
+                             cap, 1.0 / np.sqrt(D), 1, cap, ws.data_ptr(), ws.numel(), st)
+    assert rc == 0, _native.last_error()
+    np.testing.assert_array_equal(o_paged, words_of(oc))
+    gold = oracle.decode_attention(q, k, v, np.array(lens))
+    assert_bf16_parity(o_paged, gold, what=f"paged ps=16, 563 pages in one chunk ({path})")
+    tt[0, 540] = total + 5  # past both caches, inside the sequence
+    paged()
+    assert workspace_status(ws) & 0x8  # kDevBadPage
+
+
+@pytest.mark.gpu
 def test_persistence_round_trips(tmp_path):
     """driver cache -> file -> paged cache (other page size) -> file -> driver cache."""
     torch = _torch()
