@@ -665,23 +665,31 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     clocks = sampler.summary()
     o_kernel = o.clone()
 
-    # e2e: the public torch API with pinned host buffers -- the chunk's q and
-    # new K/V go host->device, the output comes back, every step
+    # e2e: the driver API with page-locked host buffers -- every step the
+    # chunk's q and new K/V go host->device and the output comes back
+    # (AttentionAccelerator.run_prefill_chunk, pipelined by sequence), after
+    # truncate_kv rewinds the previous step's append
     e2e_ms, h2d, d2h = None, 0, 0
     if not args.no_e2e:
-        qh, knh, vnh = (t.cpu().pin_memory() for t in (q, kn, vn))
-        oh = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-        qd, knd, vnd = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+        import numpy as np
+
+        from lara_b200.attn_driver import AttentionAccelerator
+
+        def pinned_words(t):
+            h = t.cpu().view(torch.int16).pin_memory()
+            return h, h.numpy().view(np.uint16)
+
+        (qh, q_np), (knh, kn_np), (vnh, vn_np) = (pinned_words(t) for t in (q, kn, vn))
+        oh, o_np = pinned_words(torch.empty_like(q))
+        lens0_np = lens0.cpu().numpy().astype(np.int32)
+        acc = AttentionAccelerator(device=local_rank)
+        acc.configure_heads(cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, max_seq_len=Lmax, batch=B)
+        acc.load_kv(k[:, :, :C].contiguous().cpu().view(torch.int16).numpy().view(np.uint16),
+                    v[:, :, :C].contiguous().cpu().view(torch.int16).numpy().view(np.uint16), lens0_np)
 
         def e2e_step():
-            qd.copy_(qh, non_blocking=True)
-            knd.copy_(knh, non_blocking=True)
-            vnd.copy_(vnh, non_blocking=True)
-            lens.copy_(lens0)
-            ops.kv_append(k, v, lens, knd, vnd, workspace=ws)
-            ops.gqa_prefill(qd, k, v, lens0, causal=True, workspace=ws, out=o)
-            oh.copy_(o, non_blocking=True)
-            stream.synchronize()
+            acc.truncate_kv(lens0_np)
+            acc.run_prefill_chunk(q_np, kn_np, vn_np, causal=True, out=o_np)
 
         for _ in range(2):
             e2e_step()
@@ -691,7 +699,8 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
         for _ in range(n_e2e):
             e2e_step()
         e2e_ms = (time.perf_counter() - t0) * 1e3 / n_e2e
-        if not torch.equal(oh.view(torch.int16), o_kernel.cpu().view(torch.int16)):
+        acc.close()
+        if not torch.equal(oh, o_kernel.cpu().view(torch.int16)):
             raise RuntimeError("API output differs from the timed kernel output")
         h2d = qh.numel() * 2 + knh.numel() * 2 + vnh.numel() * 2
         d2h = oh.numel() * 2
@@ -733,7 +742,8 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
         "e2e": None if e2e_ms is None else {
             "value": round(flops * world / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
-            "api": "ops.kv_append + ops.gqa_prefill (pinned host q, k_new, v_new, o)"},
+            "api": "AttentionAccelerator.run_prefill_chunk (page-locked host q, k_new, v_new, o; truncate_kv "
+                   "rewinds the chunk each step)"},
         "gpu_launches": args.steps * 3, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

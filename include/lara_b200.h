@@ -347,7 +347,11 @@ LARA_API int lara_kv_append_ctx(lara_ctx* ctx, const uint16_t* k_new, const uint
 
 /* Chunked prefill: append k/v_new[B][Hkv][n_new][D], then attend
  * q[B][n_new][Hq][D] -> o[B][n_new][Hq][D] over cache + self (see
- * lara_gqa_prefill); synchronous. */
+ * lara_gqa_prefill); synchronous.  With host buffers (on_device = 0), B > 1
+ * and the tensor-core kernel, the call is pipelined by sequence: the copies of
+ * one sequence overlap the kernels of the previous one and the copy back of
+ * the one before (page-locked host buffers let the copies run asynchronously).
+ * The output words are those of the single-launch path. */
 LARA_API int lara_run_prefill_chunk(lara_ctx* ctx, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
                                     uint16_t* o, int n_new, int causal, int on_device);
 
@@ -360,6 +364,14 @@ LARA_API int lara_kv_read(lara_ctx* ctx, uint16_t* k, uint16_t* v, int32_t* lens
 
 /* Copy the current lengths (host int32[B]). */
 LARA_API int lara_get_seq_lens(lara_ctx* ctx, int32_t* lens_out);
+
+/* Shorten the sequences to lens[B] (host int32, each <= its current length):
+ * the rows past the new length are dropped and later appends overwrite them
+ * (rewinding a prefill chunk or rejected speculative tokens); synchronous.
+ * LARA_ERR_STREAM_LEN if a length would grow.  No reference counterpart: the
+ * FPGA reloads its KV RAM on every transaction (sw/attn_driver.py:418-422), so
+ * it has no resident lengths to rewind. */
+LARA_API int lara_kv_truncate(lara_ctx* ctx, const int32_t* lens);
 
 /* Decode: q[B][Hq][D] -> o[B][Hq][D] over the resident cache; synchronous
  * (returns after o is written).  Page-locked host q / o (cudaHostAlloc,

@@ -118,6 +118,7 @@ SIGNATURES = {
     "lara_kv_append_ctx": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lara_run_prefill_chunk": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
     "lara_get_seq_lens": (c_int, [c_void_p, c_void_p]),
+    "lara_kv_truncate": (c_int, [c_void_p, c_void_p]),
     "lara_kv_read": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lara_run_query": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
     "lara_run_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int]),

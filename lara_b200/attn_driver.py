@@ -13,7 +13,8 @@ runs hand-written sm_100a kernels.  There is no CPU fallback; constructing an
 ``AttentionAccelerator`` without a B200 raises.
 
 Extensions (the north-star surface): ``configure_heads``, ``load_kv``,
-``append_kv``, ``run_query`` (decode), ``run_prefill_chunk``, ``read_output``.
+``append_kv``, ``run_query`` (decode), ``run_prefill_chunk``, ``read_output``;
+beyond it ``truncate_kv`` (rewind lengths), ``save_kv`` / ``restore_kv``.
 
 Arithmetic of ``run_attention``: ``"ieee"`` (default; fp32 with a true exp,
 within 2 bf16 ulp of the reference's CPU golden model) or ``"board"`` (the
@@ -579,6 +580,20 @@ class AttentionAccelerator:
             raise ValueError(f"{path}: {k.shape[2]} tokens exceed max_seq_len={self.max_seq_len}")
         self.load_kv(k, v, lens)
 
+    def truncate_kv(self, lens) -> None:
+        """Shorten the sequences to ``lens[B]`` (each at most its current length).
+
+        The rows past the new lengths are dropped and later appends overwrite
+        them: a prefill chunk or rejected speculative tokens are rewound
+        without touching the rest of the cache.  Lengths cannot grow
+        (``ValueError``)."""
+        self._require_open()
+        ln = np.ascontiguousarray(lens, dtype=np.int32)
+        if ln.shape != (self.batch,):
+            raise ValueError(f"lens must have shape ({self.batch},)")
+        check(lib.lara_kv_truncate(self._ctx, _ptr(ln)), "truncate_kv")
+        self._max_len = int(ln.max()) if ln.size else 0
+
     def append_kv(self, k_new: np.ndarray, v_new: np.ndarray) -> None:
         """Append ``k/v_new[B, Hkv, n, D]`` (or ``[B, Hkv, D]`` for one token)."""
         self._require_open()
@@ -624,12 +639,14 @@ class AttentionAccelerator:
         return out
 
     def run_prefill_chunk(self, q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, *,
-                          causal: bool = True) -> np.ndarray:
+                          causal: bool = True, out: np.ndarray | None = None) -> np.ndarray:
         """Append ``n`` new tokens and attend them over cache + self.
 
         ``q[B, n, Hq, D]`` (token-major), ``k/v_new[B, Hkv, n, D]`` ->
         ``o[B, n, Hq, D]``.  Query i of sequence b sits at position
-        ``len_b + i``; causal masking follows kv_pos <= q_pos.
+        ``len_b + i``; causal masking follows kv_pos <= q_pos.  ``out`` (a
+        contiguous uint16 array of the output shape) receives the words; with
+        page-locked inputs and output the copies overlap the kernels.
         """
         self._require_open()
         t_start = time.perf_counter()
@@ -637,7 +654,10 @@ class AttentionAccelerator:
         qw = _words("Q", q, (self.batch, n, self.n_q_heads, self.head_dim))
         kv_shape = (self.batch, self.n_kv_heads, n, self.head_dim)
         kw, vw = _words("K", k_new, kv_shape), _words("V", v_new, kv_shape)
-        out = np.empty(qw.shape, dtype=np.uint16)
+        if out is None:
+            out = np.empty(qw.shape, dtype=np.uint16)
+        elif out.shape != qw.shape or out.dtype != np.uint16 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a contiguous uint16 array of shape {qw.shape}")
         prof = self._new_profile(n, causal, 0, 0)
         self.last_profile = prof
         t = time.perf_counter()

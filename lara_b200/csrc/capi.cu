@@ -561,6 +561,9 @@ struct lara_ctx {
   bool have_perf = false;
   bool perf_pending = false;  // events of the last transaction not yet read
   bool async_pending = false; // lara_decode / lara_prefill issued, lara_sync not yet called
+  cudaStream_t copy_in = nullptr;   // pipelined host-buffer prefill: host -> device copies
+  cudaStream_t copy_out = nullptr;  // and device -> host copies
+  std::vector<cudaEvent_t> seq_ev;  // two per sequence: inputs copied, output computed
 };
 
 namespace {
@@ -666,6 +669,83 @@ int ctx_check(lara_ctx* c) {
   return LARA_OK;
 }
 
+// The copy streams and per-sequence events of the pipelined host-buffer
+// prefill, created on first use.
+int ctx_pipeline_ready(lara_ctx* c, int nseq) {
+  if (!c->copy_in) LARA_CUDA(cudaStreamCreateWithFlags(&c->copy_in, cudaStreamNonBlocking));
+  if (!c->copy_out) LARA_CUDA(cudaStreamCreateWithFlags(&c->copy_out, cudaStreamNonBlocking));
+  while ((int)c->seq_ev.size() < 2 * nseq) {
+    cudaEvent_t ev = nullptr;
+    LARA_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    c->seq_ev.push_back(ev);
+  }
+  return LARA_OK;
+}
+
+// lara_run_prefill_chunk on host buffers, pipelined by sequence: sequence b's
+// rows of q, k_new and v_new are contiguous (batch is the outer dimension), so
+// its copies in run on copy_in while the main stream appends and attends
+// sequence b - 1 and copy_out returns the output of the sequence before.  Each
+// tensor-core prefill tile belongs to one (sequence, head), so the per-sequence
+// launches write the same words as one launch over the batch.
+int prefill_chunk_pipelined(lara_ctx* c, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
+                            uint16_t* o, int n_new, int causal) {
+  int rc = ctx_pipeline_ready(c, c->batch);
+  if (rc) return rc;
+  const size_t q_seq = (size_t)n_new * c->hq * c->d;     // elements of one sequence's q (and o)
+  const size_t kv_seq = (size_t)c->hkv * n_new * c->d;   // of its k_new (and v_new)
+  const size_t cache_seq = (size_t)c->hkv * c->lmax * c->d;
+  if (c->new_cap < kv_seq * c->batch * 2) {
+    cudaFree(c->new_k); cudaFree(c->new_v);
+    c->new_k = c->new_v = nullptr; c->new_cap = 0;
+    LARA_CUDA(cudaMalloc(&c->new_k, kv_seq * c->batch * 2));
+    LARA_CUDA(cudaMalloc(&c->new_v, kv_seq * c->batch * 2));
+    c->new_cap = kv_seq * c->batch * 2;
+  }
+  cudaEvent_t* in_ev = c->seq_ev.data();
+  cudaEvent_t* out_ev = in_ev + c->batch;
+  LARA_CUDA(cudaEventRecord(c->ev[0], c->stream));
+  LARA_CUDA(cudaMemcpyAsync(c->lens_prev_dev, c->lens_dev, sizeof(int32_t) * c->batch, cudaMemcpyDeviceToDevice,
+                            c->stream));
+  LARA_CUDA(cudaStreamWaitEvent(c->copy_in, c->ev[0], 0));
+  for (int b = 0; b < c->batch; ++b) {
+    LARA_CUDA(cudaMemcpyAsync(c->pq + b * q_seq, q + b * q_seq, q_seq * 2, cudaMemcpyHostToDevice, c->copy_in));
+    LARA_CUDA(cudaMemcpyAsync(c->new_k + b * kv_seq, k_new + b * kv_seq, kv_seq * 2, cudaMemcpyHostToDevice,
+                              c->copy_in));
+    LARA_CUDA(cudaMemcpyAsync(c->new_v + b * kv_seq, v_new + b * kv_seq, kv_seq * 2, cudaMemcpyHostToDevice,
+                              c->copy_in));
+    LARA_CUDA(cudaEventRecord(in_ev[b], c->copy_in));
+  }
+  const float scale = 1.0f / std::sqrt((float)c->d);
+  for (int b = 0; b < c->batch; ++b) {
+    LARA_CUDA(cudaStreamWaitEvent(c->stream, in_ev[b], 0));
+    if (b == 0) LARA_CUDA(cudaEventRecord(c->ev[1], c->stream));
+    cudaError_t e = lara::kv_append_launch(c->k_cache + b * cache_seq, c->v_cache + b * cache_seq, c->lens_dev + b,
+                                           c->new_k + b * kv_seq, c->new_v + b * kv_seq, 1, c->hkv, c->d, c->lmax,
+                                           n_new, static_cast<int*>(c->ws), c->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+    rc = prefill_common(c->pq + b * q_seq, c->k_cache + b * cache_seq, c->v_cache + b * cache_seq,
+                        c->lens_prev_dev + b, c->po + b * q_seq, 1, n_new, c->hq, c->hkv, c->d, c->lmax, causal, scale,
+                        c->ws, c->ws_bytes, c->stream);
+    if (rc) return rc;
+    LARA_CUDA(cudaEventRecord(out_ev[b], c->stream));
+    LARA_CUDA(cudaStreamWaitEvent(c->copy_out, out_ev[b], 0));
+    LARA_CUDA(cudaMemcpyAsync(o + b * q_seq, c->po + b * q_seq, q_seq * 2, cudaMemcpyDeviceToHost, c->copy_out));
+  }
+  LARA_CUDA(cudaEventRecord(c->ev[2], c->stream));
+  // join: the main stream waits for the last copy out (in_ev[0] is free again:
+  // its wait is already enqueued)
+  LARA_CUDA(cudaEventRecord(in_ev[0], c->copy_out));
+  LARA_CUDA(cudaStreamWaitEvent(c->stream, in_ev[0], 0));
+  LARA_CUDA(cudaEventRecord(c->ev[3], c->stream));
+  for (auto& l : c->lens_host) l += n_new;
+  c->plan_valid = false;
+  rc = ctx_finish(c);
+  if (rc) return rc;
+  ctx_record_perf(c);
+  return LARA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -712,6 +792,15 @@ int lara_destroy(lara_ctx* c) {
   if (c->status_host) cudaFreeHost(c->status_host);
   for (auto& ev : c->ev)
     if (ev) cudaEventDestroy(ev);
+  for (auto& ev : c->seq_ev) cudaEventDestroy(ev);
+  if (c->copy_in) {
+    cudaStreamSynchronize(c->copy_in);
+    cudaStreamDestroy(c->copy_in);
+  }
+  if (c->copy_out) {
+    cudaStreamSynchronize(c->copy_out);
+    cudaStreamDestroy(c->copy_out);
+  }
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return LARA_OK;
@@ -841,6 +930,10 @@ int lara_run_prefill_chunk(lara_ctx* c, const uint16_t* q, const uint16_t* k_new
     LARA_CUDA(cudaMalloc(&c->po, qbytes));
     c->p_cap = qbytes;
   }
+  // host buffers on the tensor-core prefill: pipelined by sequence
+  if (!on_device && c->batch > 1 && attn_path_override() != AttnPath::kStream &&
+      lara::prefill_tc_supported(c->d, c->hq, c->hkv))
+    return prefill_chunk_pipelined(c, q, k_new, v_new, o, n_new, causal);
   LARA_CUDA(cudaEventRecord(c->ev[0], c->stream));
   LARA_CUDA(cudaMemcpyAsync(c->lens_prev_dev, c->lens_dev, sizeof(int32_t) * c->batch, cudaMemcpyDeviceToDevice,
                             c->stream));
@@ -901,6 +994,24 @@ int lara_kv_read(lara_ctx* c, uint16_t* k, uint16_t* v, int32_t* lens_out, int d
                               rows, kind, c->stream));
   LARA_CUDA(cudaStreamSynchronize(c->stream));
   for (int b = 0; b < c->batch; ++b) lens_out[b] = c->lens_host[b];
+  return LARA_OK;
+}
+
+int lara_kv_truncate(lara_ctx* c, const int32_t* lens) {
+  LARA_NVTX("lara_kv_truncate");
+  int rc = ctx_check(c);
+  if (rc) return rc;
+  if (!lens) return fail(LARA_ERR_STREAM_DEST, "null pointer");
+  for (int b = 0; b < c->batch; ++b)
+    if (lens[b] < 0 || lens[b] > c->lens_host[b])
+      return fail(LARA_ERR_STREAM_LEN, "lens[%d]=%d outside 0..%d (a truncation only shortens)", b, lens[b],
+                  c->lens_host[b]);
+  DeviceGuard g(c->device);
+  c->lens_host.assign(lens, lens + c->batch);
+  LARA_CUDA(cudaMemcpyAsync(c->lens_dev, c->lens_host.data(), sizeof(int32_t) * c->batch, cudaMemcpyHostToDevice,
+                            c->stream));
+  c->plan_valid = false;
+  LARA_CUDA(cudaStreamSynchronize(c->stream));
   return LARA_OK;
 }
 

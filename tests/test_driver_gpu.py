@@ -182,6 +182,51 @@ def test_prefill_chunk_extension():
         assert_bf16_parity(o[b].transpose(1, 0, 2), gold[0], what=f"prefill b={b}")
 
 
+def test_prefill_chunk_pinned_out_and_truncate_rewind():
+    """Host-buffer prefill is pipelined by sequence: page-locked inputs with a
+    page-locked ``out`` give the words of pageable buffers; ``truncate_kv``
+    rewinds the chunk so the same call repeats bit for bit; lengths never grow."""
+    from lara_b200.attn_driver import AttentionAccelerator
+    from lara_b200._native import LaraConfigError
+
+    rng = np.random.default_rng(17)
+    B, Hq, Hkv, D, C, n = 4, 32, 8, 128, 700, 256
+    pk = oracle.fp32_to_bf16_u16
+    k = pk(rng.standard_normal((B, Hkv, C, D)).astype(np.float32) * 0.5)
+    v = pk(rng.standard_normal((B, Hkv, C, D)).astype(np.float32) * 0.5)
+    lens = np.array([700, 1, 0, 333], np.int32)
+
+    def pinned(a):
+        t = torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).pin_memory()
+        return t, t.numpy().view(np.uint16)
+
+    qt, q = pinned(pk(rng.standard_normal((B, n, Hq, D)).astype(np.float32) * 0.5))
+    kt, kn = pinned(pk(rng.standard_normal((B, Hkv, n, D)).astype(np.float32) * 0.5))
+    vt, vn = pinned(pk(rng.standard_normal((B, Hkv, n, D)).astype(np.float32) * 0.5))
+    ot, out = pinned(np.zeros((B, n, Hq, D), np.uint16))
+    with AttentionAccelerator() as a:
+        a.configure_heads(Hq, Hkv, D, max_seq_len=1024, batch=B)
+        a.load_kv(k, v, lens)
+        o_page = a.run_prefill_chunk(q.copy(), kn.copy(), vn.copy(), causal=True).copy()
+        assert a.seq_lens.tolist() == (lens + n).tolist()
+        a.truncate_kv(lens)
+        assert a.seq_lens.tolist() == lens.tolist()
+        got = a.run_prefill_chunk(q, kn, vn, causal=True, out=out)
+        assert got is out
+        np.testing.assert_array_equal(out, o_page)
+        with pytest.raises(LaraConfigError):
+            a.truncate_kv(lens + n + 1)  # longer than the sequences
+        a.truncate_kv(lens)
+        a.append_kv(kn, vn)  # the rewound rows are overwritten by the same tokens
+        assert a.seq_lens.tolist() == (lens + n).tolist()
+    for b, c in enumerate(lens.tolist()):
+        k_all = np.concatenate([k[b:b + 1, :, :c], kn[b:b + 1]], axis=2)
+        v_all = np.concatenate([v[b:b + 1, :, :c], vn[b:b + 1]], axis=2)
+        gold = oracle.prefill_attention(q[b:b + 1].transpose(0, 2, 1, 3), k_all, v_all, np.array([c + n]), c,
+                                        causal=True)
+        assert_bf16_parity(o_page[b].transpose(1, 0, 2), gold[0], what=f"pipelined prefill b={b}")
+
+
 def test_dense_ops_matches_driver(accel):
     from lara_b200 import ops
 
