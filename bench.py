@@ -21,8 +21,9 @@ with queries/s = sequences / step time beside it.
   launch time, against the measured HBM copy bandwidth.
 * ``cpu_baseline``: the CPU oracle (restatement of the reference's
   ``cpu_attention_numpy``) on the same workload, on this host's cores.
-* ``--impl reference``: times that CPU path (the reference implementation of
-  the path is CPU code) on rank 0 and prints its own line.
+* ``--impl reference``: times that CPU path (the reference's own implementation
+  of the path is SystemVerilog RTL plus this NumPy CPU model, so the CPU model
+  is what runs here) on rank 0 and prints its own line.
 """
 
 from __future__ import annotations

@@ -1,9 +1,9 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures that pin the CPU oracle to the LARA reference.
 
-Run in a checkout that has the LARA sources (default ``/root/reference``; the
-``--reference`` flag overrides it).  The script imports the reference's own
-Python code and records its outputs:
+Run where the LARA sources are available (the ``--reference`` flag names
+the source tree).  The script imports the reference's own Python code and
+records its outputs:
 
 * ``sw/attn_driver.py:88-103`` ``fp32_to_bf16_u16`` / ``bf16_u16_to_fp32`` on a
   known-answer set of fp32 bit patterns (ties, carries, subnormals, inf, NaN)
