@@ -688,10 +688,33 @@ int ctx_pipeline_ready(lara_ctx* c, int nseq) {
 // sequence b - 1 and copy_out returns the output of the sequence before.  Each
 // tensor-core prefill tile belongs to one (sequence, head), so the per-sequence
 // launches write the same words as one launch over the batch.
+int prefill_chunk_pipelined_issue(lara_ctx* c, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
+                                  uint16_t* o, int n_new, int causal);
+
 int prefill_chunk_pipelined(lara_ctx* c, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
                             uint16_t* o, int n_new, int causal) {
   int rc = ctx_pipeline_ready(c, c->batch);
   if (rc) return rc;
+  rc = prefill_chunk_pipelined_issue(c, q, k_new, v_new, o, n_new, causal);
+  if (rc) {
+    // a failed issue may leave copies in flight on the caller's buffers: drain
+    // every stream before returning the error
+    cudaStreamSynchronize(c->copy_in);
+    cudaStreamSynchronize(c->stream);
+    cudaStreamSynchronize(c->copy_out);
+    return rc;
+  }
+  for (auto& l : c->lens_host) l += n_new;
+  c->plan_valid = false;
+  rc = ctx_finish(c);
+  if (rc) return rc;
+  ctx_record_perf(c);
+  return LARA_OK;
+}
+
+int prefill_chunk_pipelined_issue(lara_ctx* c, const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
+                                  uint16_t* o, int n_new, int causal) {
+  int rc = LARA_OK;
   const size_t q_seq = (size_t)n_new * c->hq * c->d;     // elements of one sequence's q (and o)
   const size_t kv_seq = (size_t)c->hkv * n_new * c->d;   // of its k_new (and v_new)
   const size_t cache_seq = (size_t)c->hkv * c->lmax * c->d;
@@ -738,12 +761,7 @@ int prefill_chunk_pipelined(lara_ctx* c, const uint16_t* q, const uint16_t* k_ne
   LARA_CUDA(cudaEventRecord(in_ev[0], c->copy_out));
   LARA_CUDA(cudaStreamWaitEvent(c->stream, in_ev[0], 0));
   LARA_CUDA(cudaEventRecord(c->ev[3], c->stream));
-  for (auto& l : c->lens_host) l += n_new;
-  c->plan_valid = false;
-  rc = ctx_finish(c);
-  if (rc) return rc;
-  ctx_record_perf(c);
-  return LARA_OK;
+  return rc;
 }
 
 }  // namespace
