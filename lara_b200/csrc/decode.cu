@@ -345,8 +345,17 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     for (int step = 0; step < T::kH; ++step) {
       const int off = T::kLPT >> (step + 1);
       const int nv = T::kNV >> step;
+      // two kept values per packed FADD2 (the same two round-to-nearest sums)
 #pragma unroll
-      for (int j = 0; j < nv / 2; ++j) part[j] += __shfl_xor_sync(0xffffffffu, part[j + nv / 2], off);
+      for (int j = 0; j + 1 < nv / 2; j += 2) {
+        const float2 mine = make_float2(part[j], part[j + 1]);
+        const float2 theirs = make_float2(__shfl_xor_sync(0xffffffffu, part[j + nv / 2], off),
+                                          __shfl_xor_sync(0xffffffffu, part[j + 1 + nv / 2], off));
+        const float2 sum = __fadd2_rn(mine, theirs);
+        part[j] = sum.x;
+        part[j + 1] = sum.y;
+      }
+      if ((nv / 2) & 1) part[nv / 2 - 1] += __shfl_xor_sync(0xffffffffu, part[nv - 1], off);
     }
 #pragma unroll
     for (int step = 0; step < T::kR; ++step) {
