@@ -211,6 +211,9 @@ def test_prefill_chunk_pinned_out_and_truncate_rewind():
         assert a.seq_lens.tolist() == (lens + n).tolist()
         a.truncate_kv(lens)
         assert a.seq_lens.tolist() == lens.tolist()
+        with pytest.raises(ValueError):
+            a.run_prefill_chunk(q, kn, vn, causal=True, out=np.empty((B, n, Hq, D - 1), np.uint16))
+        assert a.seq_lens.tolist() == lens.tolist()  # a rejected call appends nothing
         got = a.run_prefill_chunk(q, kn, vn, causal=True, out=out)
         assert got is out
         np.testing.assert_array_equal(out, o_page)
