@@ -283,7 +283,16 @@ LARA_API int lara_layer_prologue(const uint16_t* x, const uint16_t* rms_weight, 
  * is called.
  *  - The first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress, with that device current); make that first call
- *    before any stream capture.
+ *    before any stream capture.  The address is cached per device together
+ *    with the unique id of the CUDA context it belongs to, and looked up again
+ *    when a call runs under another context (after cudaDeviceReset, or under
+ *    a context a driver-API caller made current).
+ *  - Device-side status flags are not reported: the kernels' status word
+ *    lives in the shared array, which the caller cannot address and the next
+ *    call clears.  A seq_lens entry outside [0, max_seq_len] is clamped to
+ *    that range without an error, and a bounded wait that times out leaves
+ *    the output undefined without an error.  Callers that need those reports
+ *    use lara_gqa_decode with a workspace and lara_workspace_status.
  *  - num_splits/chunk_tokens = 0/0 plans automatically and reduces the split
  *    count until the partials fit; explicit values, or a batch whose minimum
  *    scratch exceeds the array, are rejected with LARA_ERR_RESULT_LEN and a

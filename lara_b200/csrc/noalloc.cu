@@ -14,9 +14,15 @@
 // allocating routine.
 //
 // In host code the array's name is only a host-side stand-in, never a device
-// address; its device address is looked up once per device with
-// cudaGetSymbolAddress (with that device current) on the entry point's first
-// call on that device.
+// address; its device address is looked up with cudaGetSymbolAddress (with
+// that device current) on the entry point's first call on that device, and
+// cached.  The array exists once per CUDA context, so the cache remembers the
+// unique id of the context it was looked up in (cuCtxGetId) and looks the
+// address up again when a call runs under another context: after
+// cudaDeviceReset re-creates the primary context, or when a driver-API caller
+// makes its own context current.
+#include <cuda.h>  // CUcontext / CUresult types; the entry points are fetched at run time
+
 #include <mutex>
 
 #include "../../include/lara_b200.h"
@@ -27,21 +33,58 @@ namespace {
 static __device__ __align__(256) unsigned char g_decode_scratch[LARA_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of g_decode_scratch on the current device (set-up on first use).
+struct ScratchSlot {
+  unsigned long long context_id = 0;  // 0: unknown, look the address up on every call
+  void* addr = nullptr;
+};
+
+std::mutex g_scratch_mutex;
+ScratchSlot g_scratch[kMaxDevices];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the context current on this thread; 0 when none is current yet
+// or the driver does not export the calls.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  return get_id(ctx, &id) == CUDA_SUCCESS ? id : 0;
+}
+
+// Device address of g_decode_scratch in the context current on device `dev`.
 int scratch_address(int dev, void** out) {
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_addr[dev] == nullptr) {
+  ScratchSlot& slot = g_scratch[dev];
+  const unsigned long long id = current_context_id();
+  if (slot.addr == nullptr || id == 0 || id != slot.context_id) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
     if (e != cudaSuccess || p == nullptr)
       return lara::set_last_error(LARA_ERR_CUDA, "cudaGetSymbolAddress of the no-alloc decode scratch failed: " +
                                                      std::string(cudaGetErrorString(e)));
-    g_scratch_addr[dev] = p;
+    slot.addr = p;
+    // the lookup makes the device's primary context current if none was
+    slot.context_id = id != 0 ? id : current_context_id();
   }
-  *out = g_scratch_addr[dev];
+  *out = slot.addr;
   return LARA_OK;
 }
 

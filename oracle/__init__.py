@@ -22,6 +22,7 @@ from .attention import (  # noqa: F401
     decode_attention,
     decode_attention_fp64,
     decode_partial,
+    dense_attention_fp64,
     lse_combine,
     fp32_to_bf16_u16,
     numeric_error,

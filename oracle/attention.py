@@ -92,28 +92,61 @@ def _ulp_at(mag: np.ndarray) -> np.ndarray:
     return np.ldexp(1.0, (np.floor(np.log2(m)) - 7).astype(np.int64))
 
 
-def bf16_parity_error(actual_words: np.ndarray, golden: np.ndarray) -> dict:
+def bf16_parity_error(actual_words: np.ndarray, golden: np.ndarray, fp64: np.ndarray | None = None) -> dict:
     """Error of bf16 words against golden values (fp32 or fp64), in bf16 ulp.
 
     ``max_ulp`` uses the floored ulp above (the pass criterion is
-    ``max_ulp <= PARITY_ULPS``); ``max_ulp_strict`` uses no floor.
+    ``max_ulp <= PARITY_ULPS``); ``max_ulp_strict`` uses no floor and
+    ``n_over_strict`` counts elements more than ``PARITY_ULPS`` strict ulp
+    from the golden word.
+
+    With ``fp64`` (the same attention evaluated in float64, the error
+    reference of ``sw/board_performance.py:207-219``) the fp64-anchored
+    criterion is evaluated as well: for every element
+
+        |actual - fp64| <= PARITY_ULPS * ulp(fp64) + |golden_bf16 - fp64|
+
+    with the ulp taken at the element's own fp64 magnitude (no floor), i.e.
+    the kernel is never more than 2 ulp worse than the golden model's own
+    bf16 result.  ``anchored_ratio`` is the largest left/right quotient (pass:
+    ``<= 1``), ``n_over_anchored`` the number of elements above the bound,
+    ``max_ulp_fp64_strict`` / ``golden_max_ulp_fp64_strict`` the kernel's and
+    the golden model's largest strict-ulp distance from the fp64 value.
     """
     golden_words = fp32_to_bf16_u16(np.asarray(golden, dtype=np.float32))
     g = bf16_u16_to_fp32(golden_words).astype(np.float64)
     a = bf16_u16_to_fp32(np.asarray(actual_words, dtype=np.uint16)).astype(np.float64)
     err = np.abs(a - g)
     if err.size == 0:
-        return {"max_ulp": 0.0, "max_ulp_strict": 0.0, "n_over_strict": 0, "n": 0, "finite": True}
+        out = {"max_ulp": 0.0, "max_ulp_strict": 0.0, "n_over_strict": 0, "n": 0, "finite": True}
+        if fp64 is not None:
+            out.update({"anchored_ratio": 0.0, "n_over_anchored": 0, "max_ulp_fp64_strict": 0.0,
+                        "golden_max_ulp_fp64_strict": 0.0})
+        return out
     row_max = np.max(np.abs(g), axis=-1, keepdims=True)
     floored = _ulp_at(np.maximum(np.abs(g), PARITY_FLOOR_FRAC * row_max))
     strict = _ulp_at(np.abs(g))
-    return {
+    out = {
         "max_ulp": float(np.max(err / floored)),
         "max_ulp_strict": float(np.max(err / strict)),
         "n_over_strict": int(np.count_nonzero(err > PARITY_ULPS * strict)),
         "n": int(err.size),
         "finite": bool(np.all(np.isfinite(a))),
     }
+    if fp64 is not None:
+        t = np.asarray(fp64, dtype=np.float64)
+        ulp_t = _ulp_at(np.abs(t))
+        a_err = np.abs(a - t)
+        g_err = np.abs(g - t)
+        ratio = a_err / (PARITY_ULPS * ulp_t + g_err)
+        ratio = np.where(np.isnan(ratio), np.inf, ratio)
+        out.update({
+            "anchored_ratio": float(np.max(ratio)),
+            "n_over_anchored": int(np.count_nonzero(ratio > 1.0)),
+            "max_ulp_fp64_strict": float(np.max(a_err / ulp_t)),
+            "golden_max_ulp_fp64_strict": float(np.max(g_err / ulp_t)),
+        })
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -165,6 +198,31 @@ def cpu_attention_numpy(
         scores /= np.sum(scores, axis=-1, keepdims=True)
         output[first:first + group] = np.matmul(scores, vf[g])
     return output
+
+
+def dense_attention_fp64(q: np.ndarray, k: np.ndarray, v: np.ndarray, *, causal: bool, q_pos_base: int,
+                         kv_pos_base: int, n_q_heads: int = 32, n_kv_heads: int = 8,
+                         head_dim: int = 128) -> np.ndarray:
+    """``cpu_attention_numpy``'s transaction evaluated in float64 (the error reference).
+
+    Same inputs, head map ``h // G``, scale and causal rule ``kv_pos <= q_pos``
+    (``sw/board_performance.py:174-191``); rows without a visible key give
+    zeros.  Returns float64 ``[Hq, L, D]``."""
+    group = n_q_heads // n_kv_heads
+    length = q.shape[1]
+    mask = None
+    if causal:
+        qp = q_pos_base + np.arange(length)
+        kp = kv_pos_base + np.arange(length)
+        mask = kp[np.newaxis, :] <= qp[:, np.newaxis]
+    out = np.empty((n_q_heads, length, head_dim), dtype=np.float64)
+    sc = np.float64(1.0 / np.sqrt(head_dim))
+    for g in range(n_kv_heads):
+        qf = bf16_u16_to_fp32(q[g * group:(g + 1) * group]).astype(np.float64)
+        kf = bf16_u16_to_fp32(k[g]).astype(np.float64)
+        vf = bf16_u16_to_fp32(v[g]).astype(np.float64)
+        out[g * group:(g + 1) * group] = _group_attention(qf, kf, vf, sc, mask)
+    return out
 
 
 def _group_attention(qf: np.ndarray, kf: np.ndarray, vf: np.ndarray, scale, mask=None) -> np.ndarray:

@@ -12,6 +12,19 @@ ROOT = Path(__file__).resolve().parents[1]
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 GOLDEN = ROOT / "tests" / "golden"
+
+
+def reference_root() -> Path | None:
+    """The LARA source tree named by ``LARA_REFERENCE`` (checks that read the
+    reference's own files skip when it is unset or absent)."""
+    path = os.environ.get("LARA_REFERENCE")
+    if not path:
+        return None
+    p = Path(path)
+    return p if p.is_dir() else None
+
+
+REFERENCE = reference_root()
 if str(GOLDEN) not in sys.path:
     sys.path.insert(0, str(GOLDEN))
 

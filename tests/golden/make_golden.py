@@ -26,6 +26,7 @@ sampled query rows for the larger ones, to keep the fixtures small.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import json
 import sys
@@ -88,9 +89,12 @@ def kat_bits() -> np.ndarray:
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference", help="LARA source tree")
+    ap.add_argument("--reference", default=os.environ.get("LARA_REFERENCE"),
+                    help="LARA source tree (default: $LARA_REFERENCE)")
     ap.add_argument("--out", default=str(HERE))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set LARA_REFERENCE to the LARA source tree")
     sw = Path(args.reference) / "sw"
     sys.path.insert(0, str(sw))
     import attn_driver as ref_driver  # noqa: E402  (reference code, read-only)

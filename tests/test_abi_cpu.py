@@ -12,6 +12,7 @@ from pathlib import Path
 
 import numpy as np
 import pytest
+from conftest import REFERENCE
 
 ROOT = Path(__file__).resolve().parents[1]
 HEADER = ROOT / "include" / "lara_b200.h"
@@ -183,7 +184,7 @@ def test_driver_pack_matches_kat(golden_dir):
         d.AttentionAccelerator.byte_counts(513)
 
 
-REFERENCE_SW = Path("/root/reference/sw")
+REFERENCE_SW = (REFERENCE / "sw") if REFERENCE else Path("/nonexistent-lara-reference")
 
 
 @pytest.mark.skipif(not REFERENCE_SW.is_dir(), reason="reference sources not present")

@@ -18,8 +18,9 @@ import numpy as np
 import pytest
 
 import make_board_cases as mbc
+from conftest import REFERENCE
 
-REF_SW = Path("/root/reference/sw")
+REF_SW = (REFERENCE / "sw") if REFERENCE else Path("/nonexistent-lara-reference")
 
 
 def _load(path: Path):

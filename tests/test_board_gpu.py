@@ -135,4 +135,5 @@ def test_driver_board_arithmetic(tmp_path):
     gold = oracle.cpu_attention_numpy(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
     from parity import assert_bf16_parity
 
-    assert_bf16_parity(o_ieee, gold, what="ieee after board")
+    g64 = oracle.dense_attention_fp64(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
+    assert_bf16_parity(o_ieee, gold, g64, what="ieee after board")

@@ -30,8 +30,9 @@ import pytest
 
 import oracle
 from oracle import board, board_luts
+from conftest import REFERENCE
 
-REF = Path("/root/reference/hw/data")
+REF = (REFERENCE / "hw" / "data") if REFERENCE else Path("/nonexistent-lara-reference")
 ROOT = Path(__file__).resolve().parents[1]
 
 

@@ -137,9 +137,9 @@ def test_poisoned_cache_tail(dev, monkeypatch, path):
 
 
 def test_tc_zero_length_gives_zero(tc):
-    o, gold, _, _ = _case(tc, 3, 64, 8, [0, 5, 0], 64, seed=11)
+    o, gold, g64, _ = _case(tc, 3, 64, 8, [0, 5, 0], 64, seed=11)
     assert not np.any(o[0]) and not np.any(o[2])
-    assert_bf16_parity(o[1:2], gold[1:2])
+    assert_bf16_parity(o[1:2], gold[1:2], g64[1:2])
 
 
 def test_tc_large_logits(tc):
@@ -249,9 +249,9 @@ def test_dense_transaction_on_decode_kernels(dev, monkeypatch, path):
     v = oracle.fp32_to_bf16_u16(rng.standard_normal((Hkv, L, D), dtype=np.float32))
     t = lambda a: torch.from_numpy(a.astype(np.int16)).to(dev)  # noqa: E731
     o = words_of(ops.attention_dense(t(q), t(k), t(v), causal=True, q_pos_base=31, kv_pos_base=7))
-    gold = oracle.cpu_attention_numpy(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7, n_q_heads=Hq,
-                                      n_kv_heads=Hkv, head_dim=D)
-    assert_bf16_parity(o, gold, what=f"dense {path}")
+    geo = dict(causal=True, q_pos_base=31, kv_pos_base=7, n_q_heads=Hq, n_kv_heads=Hkv, head_dim=D)
+    gold = oracle.cpu_attention_numpy(q, k, v, **geo)
+    assert_bf16_parity(o, gold, oracle.dense_attention_fp64(q, k, v, **geo), what=f"dense {path}")
 
 
 def _list_schedule_plan(lens, L, hkv, sms, overhead=1.0):

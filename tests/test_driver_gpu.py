@@ -44,11 +44,12 @@ def test_board_case_matrix(accel, golden_dir, case):
     out = accel.run_attention(q, k, v, seq_len=L, causal=causal, q_pos_base=qb, kv_pos_base=kb)
     assert out.dtype == np.uint16 and out.shape == (32, L, 128)
     rows = fx["rows"]
+    g64 = oracle.dense_attention_fp64(q, k, v, causal=causal, q_pos_base=qb, kv_pos_base=kb)
     # against the reference's own output rows
-    assert_bf16_parity(out[:, rows, :], fx["o_rows"], what=f"{name} vs reference rows")
+    assert_bf16_parity(out[:, rows, :], fx["o_rows"], g64[:, rows, :], what=f"{name} vs reference rows")
     # against the pinned oracle (full output) and fp64
     gold = oracle.cpu_attention_numpy(q, k, v, causal=causal, q_pos_base=qb, kv_pos_base=kb)
-    assert_bf16_parity(out, gold, what=f"{name} vs oracle")
+    assert_bf16_parity(out, gold, g64, what=f"{name} vs oracle")
     # harness invariants (sw/board_performance.py:345-378)
     perf = accel.read_perf()
     prof = accel.last_profile
@@ -105,8 +106,10 @@ def test_dead_causal_rows_are_zero(accel):
     q, k, v = mg.board_inputs(8, 16, oracle.fp32_to_bf16_u16)
     out = accel.run_attention(q, k, v, seq_len=16, causal=True, q_pos_base=0, kv_pos_base=8)
     assert not np.any(out[:, :8])
-    gold = oracle.prefill_attention(q[None], k[None], v[None], np.array([16]), 0, causal=True, kv_pos_base=8)[0]
-    assert_bf16_parity(out[:, 8:], gold[:, 8:])
+    args = (q[None], k[None], v[None], np.array([16]), 0)
+    gold = oracle.prefill_attention(*args, causal=True, kv_pos_base=8)[0]
+    g64 = oracle.prefill_attention(*args, causal=True, kv_pos_base=8, dtype=np.float64)[0]
+    assert_bf16_parity(out[:, 8:], gold[:, 8:], g64[:, 8:])
 
 
 def test_closed_accelerator_raises():
@@ -134,7 +137,10 @@ def test_decode_extension_cfg1(golden_dir):
         a.append_kv(fx["k_new"], fx["v_new"])
         assert a.seq_lens.tolist() == [513]
         o = a.run_query(fx["q"])
-        assert_bf16_parity(o, fx["o_fp32"], what="driver run_query cfg1")
+        k_all = np.concatenate([fx["k_cache"], fx["k_new"][:, :, None, :]], axis=2)
+        v_all = np.concatenate([fx["v_cache"], fx["v_new"][:, :, None, :]], axis=2)
+        g64 = oracle.decode_attention_fp64(fx["q"], k_all, v_all, np.array([513]))
+        assert_bf16_parity(o, fx["o_fp32"], g64, what="driver run_query cfg1")
         np.testing.assert_array_equal(a.read_output(), o)
         perf = a.read_perf()
         assert 0 <= perf["mac_cycles"] <= perf["cycles"]
@@ -155,7 +161,7 @@ def test_decode_extension_ragged_batch():
         a.load_kv(k, v, lens)
         o = a.run_query(q)
     gold = oracle.decode_attention(q, k, v, lens)
-    assert_bf16_parity(o, gold, what="ragged run_query")
+    assert_bf16_parity(o, gold, oracle.decode_attention_fp64(q, k, v, lens), what="ragged run_query")
 
 
 def test_prefill_chunk_extension():
@@ -177,9 +183,10 @@ def test_prefill_chunk_extension():
     for b, c in enumerate([C, 250]):
         k_all = np.concatenate([k[b:b + 1, :, :c], kn[b:b + 1]], axis=2)
         v_all = np.concatenate([v[b:b + 1, :, :c], vn[b:b + 1]], axis=2)
-        gold = oracle.prefill_attention(q[b:b + 1].transpose(0, 2, 1, 3), k_all, v_all, np.array([c + n]), c,
-                                        causal=True)
-        assert_bf16_parity(o[b].transpose(1, 0, 2), gold[0], what=f"prefill b={b}")
+        args = (q[b:b + 1].transpose(0, 2, 1, 3), k_all, v_all, np.array([c + n]), c)
+        gold = oracle.prefill_attention(*args, causal=True)
+        g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64)
+        assert_bf16_parity(o[b].transpose(1, 0, 2), gold[0], g64[0], what=f"prefill b={b}")
 
 
 def test_prefill_chunk_pinned_out_and_truncate_rewind():
@@ -225,9 +232,10 @@ def test_prefill_chunk_pinned_out_and_truncate_rewind():
     for b, c in enumerate(lens.tolist()):
         k_all = np.concatenate([k[b:b + 1, :, :c], kn[b:b + 1]], axis=2)
         v_all = np.concatenate([v[b:b + 1, :, :c], vn[b:b + 1]], axis=2)
-        gold = oracle.prefill_attention(q[b:b + 1].transpose(0, 2, 1, 3), k_all, v_all, np.array([c + n]), c,
-                                        causal=True)
-        assert_bf16_parity(o_page[b].transpose(1, 0, 2), gold[0], what=f"pipelined prefill b={b}")
+        args = (q[b:b + 1].transpose(0, 2, 1, 3), k_all, v_all, np.array([c + n]), c)
+        gold = oracle.prefill_attention(*args, causal=True)
+        g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64)
+        assert_bf16_parity(o_page[b].transpose(1, 0, 2), gold[0], g64[0], what=f"pipelined prefill b={b}")
 
 
 def test_dense_ops_matches_driver(accel):
@@ -262,8 +270,9 @@ def test_run_query_pinned_host_buffers_match_pageable():
         np.testing.assert_array_equal(o_pinned, o_pageable)
         perf = a.read_perf()
         assert 0 <= perf["mac_cycles"] <= perf["cycles"]
-    gold = oracle.decode_attention(q, k, v, np.array([700, 1, 350]))
-    assert_bf16_parity(o_pinned, gold, what="pinned run_query")
+    lens = np.array([700, 1, 350])
+    gold = oracle.decode_attention(q, k, v, lens)
+    assert_bf16_parity(o_pinned, gold, oracle.decode_attention_fp64(q, k, v, lens), what="pinned run_query")
 
 
 def test_run_layer_composes_prologue_and_attention():
@@ -336,7 +345,8 @@ def test_async_decode_and_prefill_match_synchronous_calls():
             if splits == 0:
                 np.testing.assert_array_equal(got, want)
             else:
-                assert_bf16_parity(got, oracle.decode_attention(q, k, v, lens), what="lara_decode splits=3")
+                assert_bf16_parity(got, oracle.decode_attention(q, k, v, lens),
+                                   oracle.decode_attention_fp64(q, k, v, lens), what="lara_decode splits=3")
         want_p = sync_acc.run_prefill_chunk(qp, kn, vn, causal=True)
         # keep the device inputs referenced until lara_sync: the call is asynchronous
         qpd, knd, vnd = t(qp), t(kn), t(vn)

@@ -66,7 +66,9 @@ def test_context_survives_a_timeout():
         with pytest.raises(TimeoutError):
             _native.check(_native.lib.lara_ctx_selftest_timeout(acc._ctx, 20_000), "selftest")
         o = acc.run_query(q)  # the context is still usable
-    assert_bf16_parity(o, oracle.decode_attention(q, k, v, np.full(B, L)), what="after timeout")
+    lens = np.full(B, L)
+    assert_bf16_parity(o, oracle.decode_attention(q, k, v, lens), oracle.decode_attention_fp64(q, k, v, lens),
+                       what="after timeout")
 
 
 def _free_port() -> int:

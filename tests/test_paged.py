@@ -129,7 +129,8 @@ def test_paged_decode_equals_contiguous(monkeypatch, page_size, geom, path):
     o_contig = words_of(ops.gqa_decode(_bf16(torch, q, dev), kc, vc, lt))
     np.testing.assert_array_equal(o_paged, o_contig)
     gold = oracle.decode_attention(q, k, v, np.array(lens))
-    assert_bf16_parity(o_paged, gold, what=f"paged ps={page_size} D={D} G={G}")
+    g64 = oracle.decode_attention_fp64(q, k, v, np.array(lens))
+    assert_bf16_parity(o_paged, gold, g64, what=f"paged ps={page_size} D={D} G={G}")
     for i, s in enumerate(slots):  # every row landed where the table says
         ks, vs = cache.gather(s)
         np.testing.assert_array_equal(words_of(ks), k[i, :, :lens[i]])
@@ -253,7 +254,8 @@ def test_paged_chunk_past_the_page_cache(monkeypatch, path):
     assert rc == 0, _native.last_error()
     np.testing.assert_array_equal(o_paged, words_of(oc))
     gold = oracle.decode_attention(q, k, v, np.array(lens))
-    assert_bf16_parity(o_paged, gold, what=f"paged ps=16, 563 pages in one chunk ({path})")
+    g64 = oracle.decode_attention_fp64(q, k, v, np.array(lens))
+    assert_bf16_parity(o_paged, gold, g64, what=f"paged ps=16, 563 pages in one chunk ({path})")
     tt[0, 540] = total + 5  # past both caches, inside the sequence
     paged()
     assert workspace_status(ws) & 0x8  # kDevBadPage

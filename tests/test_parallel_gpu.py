@@ -44,8 +44,9 @@ def test_split_kv_world1_matches_oracle():
     lens = torch.full((B,), L, dtype=torch.int32, device=dev)
     dec = parallel.SplitKVDecoder(B, HQ, HKV, D, L, dev)
     o = dec(q, k, v, lens)
-    gold = oracle.decode_attention(words_of(q), words_of(k), words_of(v), np.full(B, L))
-    assert_bf16_parity(words_of(o), gold, what="split-kv world 1")
+    args = (words_of(q), words_of(k), words_of(v), np.full(B, L))
+    gold = oracle.decode_attention(*args)
+    assert_bf16_parity(words_of(o), gold, oracle.decode_attention_fp64(*args), what="split-kv world 1")
 
 
 def _rank_main(rank, world, port, q_out):
@@ -68,10 +69,11 @@ def _rank_main(rank, world, port, q_out):
         full = ops.Decoder(B, HQ, HKV, D, L, dev)(q, k, v, torch.full((B,), L, dtype=torch.int32, device=dev))
         torch.cuda.synchronize(dev)
         if rank == 0:
-            gold = oracle.decode_attention(words_of(q), words_of(k), words_of(v), np.full(B, L))
-            e_gold = oracle.bf16_parity_error(words_of(o), gold)
+            args = (words_of(q), words_of(k), words_of(v), np.full(B, L))
+            gold = oracle.decode_attention(*args)
+            e_gold = oracle.bf16_parity_error(words_of(o), gold, oracle.decode_attention_fp64(*args))
             e_full = oracle.bf16_parity_error(words_of(o), oracle.bf16_u16_to_fp32(words_of(full)))
-            q_out.put((e_gold["max_ulp"], e_full["max_ulp"]))
+            q_out.put((e_gold["max_ulp"], e_full["max_ulp"], e_gold["n_over_anchored"]))
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
@@ -93,5 +95,6 @@ def test_split_kv_two_gpus_nccl():
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
-    ulp_gold, ulp_full = q_out.get(timeout=10)
+    ulp_gold, ulp_full, n_over = q_out.get(timeout=10)
     assert ulp_gold <= oracle.PARITY_ULPS and ulp_full <= oracle.PARITY_ULPS, (ulp_gold, ulp_full)
+    assert n_over == 0, f"fp64-anchored bound exceeded on {n_over} elements"

@@ -128,31 +128,63 @@ def test_dense_tc_matches_stream(monkeypatch):
         monkeypatch.setenv("LARA_ATTN_PATH", path)
         outs[path] = words_of(ops.attention_dense(t(q), t(k), t(v), causal=True, q_pos_base=31, kv_pos_base=7))
     gold = oracle.cpu_attention_numpy(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
+    g64 = oracle.dense_attention_fp64(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
     for path, o in outs.items():
-        assert_bf16_parity(o, gold, what=f"dense {path}")
+        assert_bf16_parity(o, gold, g64, what=f"dense {path}")
 
 
 @pytest.mark.slow
 def test_config5_full_size_sampled(monkeypatch):
-    """Config 5 (B=4, 2048 new over 8192 cached, causal) on the tensor-core path;
-    oracle on query rows 0-15 and 2032-2047 of every sequence."""
+    """Config 5 (B=4, 2048 new tokens over 8192 cached, causal) through the
+    context API on device buffers: ``lara_kv_load`` of the cached tokens, then
+    ``lara_prefill`` appends the new K/V and attends on the tensor-core path.
+    The appended cache rows are read back (``lara_kv_read``) and must equal the
+    new K/V word for word; the output is checked against the oracle (golden
+    and fp64-anchored bounds) on the rows either side of every 128-row query
+    tile boundary (0, 127/128, ..., 1919/1920, 2047) of every sequence, which
+    covers the first and last row of every causal diagonal tile."""
+    import ctypes
+
+    from lara_b200 import _native
+    from lara_b200.attn_driver import AttentionAccelerator
     from lara_b200.workloads import PREFILL, make_prefill_inputs
 
     monkeypatch.setenv("LARA_ATTN_PATH", "tc")
     dev = torch.device("cuda:0")
     cfg = PREFILL
     q, k, v, kn, vn, lens = make_prefill_inputs(cfg, dev)
-    C, n = cfg.cached, cfg.new
-    k[:, :, C:C + n] = kn
-    v[:, :, C:C + n] = vn
-    o = words_of(_prefill(dev, q, k, v, [C] * cfg.batch, True))
-    qw = words_of(q)
-    for b in range(cfg.batch):
-        kw, vw = words_of(k[b:b + 1]), words_of(v[b:b + 1])
-        for i0 in (0, n - 16):
-            qs = qw[b:b + 1, i0:i0 + 16].transpose(0, 2, 1, 3)
-            gold = oracle.prefill_attention(qs, kw, vw, np.array([C + n]), C + i0, causal=True)[0]
-            assert_bf16_parity(o[b, i0:i0 + 16].transpose(1, 0, 2), gold, what=f"cfg5 b={b} rows {i0}+16")
+    B, C, n = cfg.batch, cfg.cached, cfg.new
+    Hq, Hkv, D = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim
+    lib = _native.lib
+    o = torch.empty_like(q)
+    lens_np = np.full(B, C, np.int32)
+    with AttentionAccelerator() as acc:
+        acc.configure_heads(Hq, Hkv, D, max_seq_len=C + n, batch=B)
+        _native.check(lib.lara_kv_load(acc._ctx, k.data_ptr(), v.data_ptr(),
+                                       lens_np.ctypes.data_as(ctypes.c_void_p), C + n, 1), "kv_load")
+        torch.cuda.synchronize()
+        _native.check(lib.lara_prefill(acc._ctx, q.data_ptr(), kn.data_ptr(), vn.data_ptr(), o.data_ptr(), n, 1,
+                                       torch.cuda.current_stream().cuda_stream), "lara_prefill")
+        _native.check(lib.lara_sync(acc._ctx, 60_000), "lara_sync")
+        assert acc.seq_lens.tolist() == [C + n] * B
+        k_back, v_back = torch.empty_like(k), torch.empty_like(v)
+        lens_back = np.zeros(B, np.int32)
+        _native.check(lib.lara_kv_read(acc._ctx, k_back.data_ptr(), v_back.data_ptr(),
+                                       lens_back.ctypes.data_as(ctypes.c_void_p), C + n, 1), "kv_read")
+    assert lens_back.tolist() == [C + n] * B
+    assert torch.equal(k_back[:, :, C:].view(torch.int16), kn.view(torch.int16))
+    assert torch.equal(v_back[:, :, C:].view(torch.int16), vn.view(torch.int16))
+    assert torch.equal(k_back[:, :, :C].view(torch.int16), k[:, :, :C].view(torch.int16))
+    ow, qw = words_of(o), words_of(q)
+    starts = [0] + [t * 128 - 1 for t in range(1, n // 128)] + [n - 2]
+    for b in range(B):
+        kw, vw = words_of(k_back[b:b + 1]), words_of(v_back[b:b + 1])
+        for i0 in starts:
+            qs = qw[b:b + 1, i0:i0 + 2].transpose(0, 2, 1, 3)
+            args = (qs, kw, vw, np.array([C + n]), C + i0)
+            gold = oracle.prefill_attention(*args, causal=True)[0]
+            g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64)[0]
+            assert_bf16_parity(ow[b, i0:i0 + 2].transpose(1, 0, 2), gold, g64, what=f"cfg5 b={b} rows {i0}+2")
 
 
 def test_ops_gqa_prefill_matches_abi():

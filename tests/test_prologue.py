@@ -21,8 +21,9 @@ import pytest
 
 import oracle
 from oracle import prologue
+from conftest import REFERENCE
 
-REF_THETA = Path("/root/reference/hw/data/rope_theta.hex")
+REF_THETA = (REFERENCE / "hw" / "data" / "rope_theta.hex") if REFERENCE else Path("/nonexistent-lara-reference")
 # SHA-256 of hw/data/rope_theta.hex's 64 words (little-endian uint32)
 THETA_SHA256 = "517d37a3dd07d63acf7d03dc05ff2e4f3a778c2783e9541d86ef1cd37bb5b968"
 

@@ -15,6 +15,7 @@ rest of the suite.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import numpy as np
@@ -64,8 +65,9 @@ def test_noalloc_matches_workspace_entry_point_twice(geom):
         torch.cuda.synchronize()
         assert_bf16_parity(words_of(o), golden, what=f"no-alloc call {call + 1}")
     # and against the CPU oracle, as for every decode path
-    gold = oracle.decode_attention(words_of(q), words_of(k), words_of(v), np.asarray(lens_list))
-    assert_bf16_parity(words_of(o), gold, what="no-alloc vs oracle")
+    args = (words_of(q), words_of(k), words_of(v), np.asarray(lens_list))
+    gold = oracle.decode_attention(*args)
+    assert_bf16_parity(words_of(o), gold, oracle.decode_attention_fp64(*args), what="no-alloc vs oracle")
 
 
 def test_noalloc_forced_splits_then_other_shape():
@@ -80,7 +82,8 @@ def test_noalloc_forced_splits_then_other_shape():
     o = torch.empty_like(q)
     assert _noalloc(_native.lib, q, k, v, lens, o, 2, 32, 8, 128, 4096, 8, 512) == 0, _native.last_error()
     torch.cuda.synchronize()
-    assert_bf16_parity(words_of(o), oracle.bf16_u16_to_fp32(words_of(exp)), what="forced splits")
+    # the same plan runs the same kernel on the same inputs: the same words
+    np.testing.assert_array_equal(words_of(o), words_of(exp))
     q2, k2, v2 = _inputs(dev, 5, 64, 8, 128, 1000, seed=6)
     lens2 = torch.tensor([1000, 7, 999, 64, 500], dtype=torch.int32, device=dev)
     exp2 = ops.Decoder(5, 64, 8, 128, 1000, dev)(q2, k2, v2, lens2)
@@ -101,3 +104,58 @@ def test_noalloc_rejects_sizes_beyond_the_scratch():
     rc = _noalloc(_native.lib, q, k, v, lens, o, 64, 32, 8, 128, 256, 64, 64)
     assert rc == _native.LARA_ERR_RESULT_LEN
     assert "no-alloc scratch" in _native.last_error()
+
+
+def _stage_tokens(head_dim, group):
+    """Tokens per pipeline stage of the CUDA-core decode kernel, the split-chunk
+    granule (``Traits<D, G>::kTile`` in lara_b200/csrc/decode.cu)."""
+    vec = 4 if group >= 8 else 8
+    lanes = head_dim // vec
+    rows = 32 // lanes
+    passes = max(1, min(4, lanes // group))
+    return 8 * passes * rows
+
+
+def test_noalloc_reduces_a_plan_that_does_not_fit():
+    """The one path of its own: with splits = chunk = 0, a workload whose
+    planned split partials exceed LARA_NOALLOC_SCRATCH_BYTES is re-planned with
+    fewer splits until they fit.  The result must equal, word for word, the
+    workspace entry point run with that reduced plan, and meet the oracle."""
+    from lara_b200 import _native, ops
+
+    lib = _native.lib
+    cap = 8 * 1024 * 1024
+    dev = torch.device("cuda:0")
+    Hq, Hkv, D = 64, 8, 128
+    chosen = None
+    for B, L in ((64, 32768), (128, 16384), (256, 8192), (256, 16384)):
+        s_, c_ = ctypes.c_int(0), ctypes.c_int(0)
+        assert lib.lara_decode_plan(B, Hq, Hkv, D, L, None, ctypes.byref(s_), ctypes.byref(c_)) == 0
+        if lib.lara_decode_workspace_bytes(B, Hq, Hkv, D, s_.value) > cap:
+            chosen = (B, L, s_.value, c_.value)
+            break
+    assert chosen is not None, "no candidate workload plans more split partials than the scratch holds"
+    B, L, splits, chunk = chosen
+    planned = splits
+    tile = _stage_tokens(D, Hq // Hkv)
+    while splits > 1 and lib.lara_decode_workspace_bytes(B, Hq, Hkv, D, splits) > cap:
+        splits -= 1
+        chunk = -(-L // (tile * splits)) * tile
+        splits = -(-L // chunk)
+    assert splits < planned and lib.lara_decode_workspace_bytes(B, Hq, Hkv, D, splits) <= cap
+    q, k, v = _inputs(dev, B, Hq, Hkv, D, L, seed=9)
+    lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+    exp = ops.Decoder(B, Hq, Hkv, D, L, dev, num_splits=splits, chunk_tokens=chunk)(q, k, v, lens)
+    o = torch.empty_like(q)
+    assert _noalloc(lib, q, k, v, lens, o, B, Hq, Hkv, D, L) == 0, _native.last_error()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(words_of(o), words_of(exp))
+    qw, ow = words_of(q), words_of(o)
+    G = Hq // Hkv
+    for b, h in ((0, 0), (B // 2, 3), (B - 1, Hkv - 1)):
+        kw, vw = words_of(k[b:b + 1, h:h + 1]), words_of(v[b:b + 1, h:h + 1])
+        qs = qw[b:b + 1, h * G:(h + 1) * G]
+        gold = oracle.decode_attention(qs, kw, vw, np.array([L]))
+        g64 = oracle.decode_attention_fp64(qs, kw, vw, np.array([L]))
+        assert_bf16_parity(ow[b, h * G:(h + 1) * G], gold[0], g64[0],
+                           what=f"no-alloc reduced plan {planned} -> {splits} splits b={b} kvh={h}")
