@@ -15,6 +15,13 @@ for each sequence K then V (whole [Hkv, L, D] blocks), then new K/V rows.
 4. long-context split-KV: B=8, 32/8 heads, D=128, L=1,048,576, N(0,1)*0.5, seed 3;
 5. chunked prefill: B=4, 2048 new tokens over 8192 cached (causal), 32/8
    heads, D=128, N(0,1)*0.5, seed 4.
+
+``make_decode_inputs`` / ``make_prefill_inputs`` draw a whole workload from
+one generator (the tests' inputs).  The sharded forms ``decode_shard`` /
+``prefill_shard`` (the benchmark's inputs) draw every piece from its own
+generator keyed by (seed, tensor, sequence, token block), so a sequence's --
+or a token range's -- words are the same whichever rank holds it and however
+many ranks there are, and any rank can redraw any piece to check it.
 """
 
 from __future__ import annotations
@@ -153,3 +160,125 @@ def make_prefill_inputs(cfg: PrefillConfig, device, *, batch: int | None = None,
     v_new = (torch.randn((B, Hkv, n, D), generator=g, device=dev) * cfg.std).to(torch.bfloat16)
     lens = torch.full((B,), C, dtype=torch.int32, device=dev)
     return q, k, v, k_new, v_new, lens
+
+
+# ---------------------------------------------------------------------------
+# sharded, rank-independent draws (benchmark inputs)
+# ---------------------------------------------------------------------------
+
+TOKEN_BLOCK = 65536  # tokens per generator stream of a (sequence, K or V) row
+_Q, _K, _V, _KNEW, _VNEW = 1, 2, 3, 4, 5
+
+
+def _generator(device, *key):
+    """A device generator seeded from a tuple of small ints."""
+    import torch
+
+    seed = 0
+    for x in key:
+        seed = (seed * 1_000_003 + int(x)) % (2 ** 61 - 1)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def _draw_rows(cfg, device, kind: int, b: int, start: int, count: int, total: int, std: float,
+               heads: int, boost=None):
+    """fp32 rows [heads, count, D] of token range [start, start+count) of one
+    sequence whose row holds ``total`` tokens: token block j of the row comes
+    from generator (seed, kind, b, j) as N(0,1)*std [, K channels boosted]."""
+    import torch
+
+    D = cfg.head_dim
+    out = torch.empty((heads, count, D), dtype=torch.float32, device=device)
+    j = start // TOKEN_BLOCK
+    while count > 0 and j * TOKEN_BLOCK < start + count:
+        b0 = j * TOKEN_BLOCK
+        n = min(TOKEN_BLOCK, total - b0)
+        blk = torch.randn((heads, n, D), generator=_generator(device, cfg.seed, kind, b, j), device=device) * std
+        if boost is not None:
+            blk *= boost
+        lo, hi = max(start, b0), min(start + count, b0 + n)
+        out[:, lo - start:hi - start] = blk[:, lo - b0:hi - b0]
+        j += 1
+    return out
+
+
+def decode_shard(cfg: DecodeConfig, device, seqs, lens_all, *, token_start: int = 0, token_count=None,
+                 capacity=None):
+    """Decode inputs of the global sequences ``seqs`` (indices into the
+    workload's batch, lengths ``lens_all[b]``), restricted to the token range
+    [token_start, token_start + token_count) of every sequence (a split-KV
+    rank's slice; default: every token).
+
+    Returns q [len(seqs), Hq, D], k/v [len(seqs), Hkv, capacity, D] (rows past
+    a sequence's slice zeroed) and the int32 slice lengths, all on ``device``."""
+    import torch
+
+    dev = torch.device(device)
+    Hq, Hkv, D = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim
+    lens_all = np.asarray(lens_all)
+    local = []
+    for b in seqs:
+        total = int(lens_all[b])
+        cnt = total - token_start if token_count is None else min(int(token_count), total - token_start)
+        local.append(max(0, cnt))
+    cap = max(1, max(local) if capacity is None else int(capacity))
+    boost = None
+    if cfg.k_boost_channels:
+        boost = torch.ones(D, device=dev)
+        for ch in cfg.k_boost_channels:
+            boost[ch] = cfg.k_boost
+    q = torch.empty((len(seqs), Hq, D), dtype=torch.bfloat16, device=dev)
+    k = torch.zeros((len(seqs), Hkv, cap, D), dtype=torch.bfloat16, device=dev)
+    v = torch.zeros_like(k)
+    for i, b in enumerate(seqs):
+        q[i] = (torch.randn((Hq, D), generator=_generator(dev, cfg.seed, _Q, b), device=dev) * cfg.std).to(
+            torch.bfloat16)
+        n, total = local[i], int(lens_all[b])
+        if n > 0:
+            k[i, :, :n] = _draw_rows(cfg, dev, _K, b, token_start, n, total, cfg.std, Hkv, boost).to(torch.bfloat16)
+            v[i, :, :n] = _draw_rows(cfg, dev, _V, b, token_start, n, total, cfg.std, Hkv).to(torch.bfloat16)
+    return q, k, v, torch.tensor(local, dtype=torch.int32, device=dev)
+
+
+def prefill_units(cfg: PrefillConfig, world: int, rank: int):
+    """Rank's share of the prefill's (sequence, kv head) units: a contiguous
+    range of the B * Hkv units, returned as [(sequence, first kv head, kv
+    heads)] pieces (one per sequence the range touches)."""
+    units = cfg.batch * cfg.n_kv_heads
+    base, rem = divmod(units, world)
+    u0 = rank * base + min(rank, rem)
+    u1 = u0 + base + (1 if rank < rem else 0)
+    pieces = []
+    u = u0
+    while u < u1:
+        b, h = divmod(u, cfg.n_kv_heads)
+        n = min(u1 - u, cfg.n_kv_heads - h)
+        pieces.append((b, h, n))
+        u += n
+    return pieces
+
+
+def prefill_shard(cfg: PrefillConfig, device, b: int, h0: int, nh: int):
+    """Chunked-prefill inputs of kv heads [h0, h0+nh) of sequence b (and their
+    query heads): q [1, n, nh*G, D], cache k/v [1, nh, C+n, D] with the first C
+    tokens drawn, new k/v [1, nh, n, D], cached length [C].  Each (sequence,
+    tensor) is one generator stream over all heads, sliced to the rank's heads."""
+    import torch
+
+    dev = torch.device(device)
+    G, D, C, n = cfg.n_q_heads // cfg.n_kv_heads, cfg.head_dim, cfg.cached, cfg.new
+    Hq, Hkv = cfg.n_q_heads, cfg.n_kv_heads
+
+    def draw(kind, shape):
+        return torch.randn(shape, generator=_generator(dev, cfg.seed, kind, b), device=dev) * cfg.std
+
+    q = draw(_Q, (n, Hq, D))[:, h0 * G:(h0 + nh) * G].to(torch.bfloat16).unsqueeze(0).contiguous()
+    k = torch.zeros((1, nh, C + n, D), dtype=torch.bfloat16, device=dev)
+    v = torch.zeros_like(k)
+    k[0, :, :C] = draw(_K, (Hkv, C, D))[h0:h0 + nh].to(torch.bfloat16)
+    v[0, :, :C] = draw(_V, (Hkv, C, D))[h0:h0 + nh].to(torch.bfloat16)
+    kn = draw(_KNEW, (Hkv, n, D))[h0:h0 + nh].to(torch.bfloat16).unsqueeze(0).contiguous()
+    vn = draw(_VNEW, (Hkv, n, D))[h0:h0 + nh].to(torch.bfloat16).unsqueeze(0).contiguous()
+    return q, k, v, kn, vn, torch.tensor([C], dtype=torch.int32, device=dev)
