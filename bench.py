@@ -373,12 +373,13 @@ class ParityTally:
 
     def __init__(self):
         self.r = {"groups": 0, "elements": 0, "max_ulp": 0.0, "max_ulp_strict": 0.0, "n_over_strict": 0,
-                  "anchored_ratio": 0.0, "n_over_anchored": 0, "finite": True}
+                  "anchored_ratio": 0.0, "n_over_anchored": 0, "n_over_plain": 0, "excess_kappa_u": 0.0,
+                  "eps_golden_u": 0.0, "finite": True}
 
-    def add(self, got_words, gold, g64):
+    def add(self, got_words, gold, g64, tensor_core: bool = False):
         import oracle
 
-        e = oracle.bf16_parity_error(got_words, gold, g64)
+        e = oracle.bf16_parity_error(got_words, gold, g64, oracle.TC_SPLIT_P_KAPPA if tensor_core else 0.0)
         r = self.r
         r["groups"] += 1
         r["elements"] += e["n"]
@@ -387,6 +388,9 @@ class ParityTally:
         r["n_over_strict"] += e["n_over_strict"]
         r["anchored_ratio"] = max(r["anchored_ratio"], e["anchored_ratio"])
         r["n_over_anchored"] += e["n_over_anchored"]
+        r["n_over_plain"] += e["n_over_plain"]
+        r["excess_kappa_u"] = max(r["excess_kappa_u"], e["excess_kappa_u"])
+        r["eps_golden_u"] = max(r["eps_golden_u"], e["eps_golden_u"])
         r["finite"] = r["finite"] and e["finite"]
 
     def result(self, what: str) -> dict:
@@ -402,7 +406,7 @@ class ParityTally:
         return r
 
 
-def check_decode_groups(cfg, pairs, q_local, seqs, o_local, kv_rows) -> ParityTally:
+def check_decode_groups(cfg, pairs, q_local, seqs, o_local, kv_rows, tensor_core: bool) -> ParityTally:
     """Oracle check of decode outputs: for each (local index, kv head), the G
     query heads of that group.  kv_rows(i, h) returns the sequence's full K/V
     rows of head h as device tensors [n, D]."""
@@ -419,7 +423,7 @@ def check_decode_groups(cfg, pairs, q_local, seqs, o_local, kv_rows) -> ParityTa
         qs = qw[i:i + 1, h * G:(h + 1) * G]
         gold = oracle.decode_attention(qs, kw, vw, np.array([n]))
         g64 = oracle.decode_attention_fp64(qs, kw, vw, np.array([n]))
-        tally.add(ow[i, h * G:(h + 1) * G], gold[0], g64[0])
+        tally.add(ow[i, h * G:(h + 1) * G], gold[0], g64[0], tensor_core)
     return tally
 
 
@@ -540,7 +544,8 @@ def decode_record(args, cfgnum: int, rank: int, world: int, dev, comm: Collectiv
                 pairs = [(i, seqs[i] % Hkv) for i in pick]
             else:
                 pairs = sorted({(0, 0), (0, Hkv - 3), (B // 2, Hkv // 2), (B - 1, Hkv - 1)})
-        parity = check_decode_groups(cfg, pairs, q, seqs, o, kv_rows).result(
+        on_tc = ops.decode_kernel(Hq, Hkv, D) == "tensor"
+        parity = check_decode_groups(cfg, pairs, q, seqs, o, kv_rows, on_tc).result(
             f"{len(pairs)} (sequence, kv head) groups of rank 0: {[(seqs[i], h) for i, h in pairs]}")
     comm.barrier()
     rec = {
@@ -761,8 +766,8 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
             qs = qw[:, i0:i0 + 2].transpose(0, 2, 1, 3)
             args_ = (qs, kw_all, vw_all, np.array([C + n]), C + i0)
             gold = oracle.prefill_attention(*args_, causal=True)[0]
-            g64 = oracle.prefill_attention(*args_, causal=True, dtype=np.float64)[0]
-            tally.add(ow[0, i0:i0 + 2].transpose(1, 0, 2), gold, g64)
+            g64 = oracle.prefill_attention(*args_, causal=True, dtype=np.float64, kappa=True)[0]
+            tally.add(ow[0, i0:i0 + 2].transpose(1, 0, 2), gold, g64, os.environ.get("LARA_ATTN_PATH") != "stream")
         parity = tally.result(f"query rows 127-128 and {n - 2}-{n - 1} of sequence {p['b']}, kv heads "
                               f"{p['h0']}..{p['h0'] + p['nh'] - 1} (all their query heads); appended K/V compared "
                               f"word for word")

@@ -118,7 +118,7 @@ int decode_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, const
   p.part_acc = reinterpret_cast<float*>(base + w.acc_off);
   p.out_ml = out_ml; p.out_acc = out_acc;
   p.block_table = block_table; p.page_log2 = page_log2; p.pages_per_seq = pages_per_seq; p.num_pages = num_pages;
-  p.chunk0 = lara::decode_first_chunk(nsplit, chunk, hq / hkv, d);
+  p.chunk0 = lara::decode_first_chunk(nsplit, chunk, hq / hkv, d, (long long)batch * hkv);
   cudaError_t e = lara::decode_launch(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return LARA_OK;

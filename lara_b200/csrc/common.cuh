@@ -29,6 +29,20 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---- programmatic dependent launch ------------------------------------------
+// A kernel launched by launch_with_pdl() may start while the kernel before it
+// in the stream is still running.  It calls allow_dependent_launch() on entry
+// (the next kernel may then be scheduled once every CTA of this grid has
+// started) and grid_dependency_wait() before its first global-memory access:
+// that wait returns once the previous grid has completed and its writes are
+// visible.  Launched without the attribute, both are no-ops.
+
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- mbarrier ---------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

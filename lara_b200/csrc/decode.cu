@@ -33,6 +33,7 @@
 //    partials and writes the bf16 output.
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -181,6 +182,44 @@ __device__ __forceinline__ void issue_tile(uint8_t* smem, uint64_t* full, int t,
   }
 }
 
+// Paged caches, issued by a whole warp (every lane calls this): a tile inside
+// one page takes lane 0's two copies; a tile split over pages shorter than a
+// tile gives each (page piece, K or V) copy to its own lane, so the refill
+// costs one copy's issue latency instead of 2 x pieces in a row.
+template <int D, int G>
+__device__ __forceinline__ void issue_tile_paged_warp(uint8_t* smem, uint64_t* full, int t, int ntok,
+                                                      const DecodeParams& p, int seq, int kvh, int tok_begin,
+                                                      const long long* pbase, uint64_t pol, int lane,
+                                                      long long pre_base = -1) {
+  using T = Traits<D, G>;
+  const int n = min(T::kTile, ntok - t * T::kTile);
+  const int ps = 1 << p.page_log2;
+  const int tok0 = tok_begin + t * T::kTile;
+  if (n <= ps - (tok0 & (ps - 1))) {
+    if (lane == 0) issue_tile<D, G, true>(smem, full, t, ntok, p, seq, kvh, tok_begin, pbase, pol, pre_base);
+    return;
+  }
+  const int st = t % T::kStages;
+  uint8_t* stage = smem + st * T::kStageBytes;
+  if (lane == 0) mbar_arrive_expect_tx(&full[st], 2u * (uint32_t)n * T::kRowBytes);
+  __syncwarp();
+  // the tile starts on a page boundary; piece i is the first cnt rows of cached page idx0 + i
+  const int pieces = (n + ps - 1) >> p.page_log2;
+  const int i = lane >> 1;
+  if (i < pieces) {
+    const int r = i << p.page_log2;
+    const int cnt = min(n - r, ps);
+    const int idx = (tok0 >> p.page_log2) - (tok_begin >> p.page_log2) + i;
+    const long long off = idx < kPageCacheEntries
+                              ? pbase[idx]
+                              : page_block_uncached(p.block_table, p.pages_per_seq, p.page_log2, p.num_pages,
+                                                    p.n_kv_heads, p.status, seq, kvh, tok0 + r, D);
+    const int half = lane & 1;
+    bulk_g2s(stage + half * T::kHalfStage + r * T::kRowBytes, (half ? p.v : p.k) + off,
+             (uint32_t)cnt * T::kRowBytes, &full[st], pol);
+  }
+}
+
 // kPaged: K/V in a page pool addressed through the block table; each cache
 // layout gets its own instantiation, so a kernel holds only the copy code it runs.
 template <int D, int G, bool kPaged>
@@ -201,6 +240,8 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   const int lane = threadIdx.x & 31;
   const bool partial_out = p.out_acc != nullptr;
 
+  allow_dependent_launch();
+  grid_dependency_wait();  // the previous kernel's writes (q, lengths, cache, workspace) are visible from here
   const int len = seq_len_of(p, seq, b - seq * p.rows_per_seq);
   // split 0 covers [0, c0), split s >= 1 covers [c0 + (s-1)*chunk, c0 + s*chunk)
   const int c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
@@ -259,9 +300,20 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     flag[1] = 0;  // last-CTA broadcast
     flag[2] = 0;  // tiles issued
     mbar_fence_init();
-    const int first = ntiles < T::kStages ? ntiles : T::kStages;
-    for (int t = 0; t < first; ++t) issue_tile<D, G, kPaged>(smem, full, t, ntok, p, seq, kvh, tok_begin, pbase, pol);
-    flag[2] = first;
+    if constexpr (!kPaged) {
+      const int first = ntiles < T::kStages ? ntiles : T::kStages;
+      for (int t = 0; t < first; ++t) issue_tile<D, G, false>(smem, full, t, ntok, p, seq, kvh, tok_begin, pbase, pol);
+      flag[2] = first;
+    }
+  }
+  if constexpr (kPaged) {
+    if (warp == 0) {
+      __syncwarp();  // lane 0's barrier initialisation is visible to the warp
+      const int first = ntiles < T::kStages ? ntiles : T::kStages;
+      for (int t = 0; t < first; ++t)
+        issue_tile_paged_warp<D, G>(smem, full, t, ntok, p, seq, kvh, tok_begin, pbase, pol, lane);
+      if (lane == 0) flag[2] = first;
+    }
   }
   __syncthreads();
 
@@ -430,12 +482,24 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     // then observes the release complete (test_wait: acquire) claims the
     // refill of tile i + kStages with one CAS; nobody blocks on it.
     __syncwarp();
-    if (lane == 0) {
+    if constexpr (kPaged) {
+      const int nxt = i + T::kStages;
+      int claim = 0;
+      if (lane == 0) {
+        mbar_arrive(&empty[st]);
+        claim = nxt < ntiles && mbar_test_wait(&empty[st], round & 1) &&
+                atomicCAS(&refill_round[st], round, round + 1) == round;
+      }
+      if (__shfl_sync(0xffffffffu, claim, 0)) {
+        issue_tile_paged_warp<D, G>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pbase, pol, lane, pre_base);
+        if (lane == 0) atomicMax(&flag[2], nxt + 1);
+      }
+    } else if (lane == 0) {
       mbar_arrive(&empty[st]);
       const int nxt = i + T::kStages;
       if (nxt < ntiles && mbar_test_wait(&empty[st], round & 1) &&
           atomicCAS(&refill_round[st], round, round + 1) == round) {
-        issue_tile<D, G, kPaged>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pbase, pol, pre_base);
+        issue_tile<D, G, false>(smem, full, nxt, ntok, p, seq, kvh, tok_begin, pbase, pol, pre_base);
         atomicMax(&flag[2], nxt + 1);
       }
     }
@@ -588,6 +652,25 @@ int device_sm_count() {
   return n;
 }
 
+cudaError_t launch_with_pdl(const void* fn, dim3 grid, dim3 block, void** args, size_t smem, cudaStream_t stream) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("LARA_PDL");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled) return cudaLaunchKernel(fn, grid, block, args, smem, stream);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 int decode_tile_tokens(int head_dim, int group) { return lookup(head_dim, group).tile; }
 
 int decode_chunk_granule(int head_dim, int group) {
@@ -668,8 +751,9 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
   *chunk_out = best_chunk;
 }
 
-int decode_first_chunk(int nsplit, int chunk, int group, int head_dim) {
+int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long units) {
   if (nsplit != 2 || decode_tc_selected(head_dim, group)) return 0;
+  if (units < device_sm_count()) return 0;
   const int tile = decode_tile_tokens(head_dim, group);
   if (tile <= 0) return 0;
   const long long span = 2ll * chunk;
@@ -709,7 +793,7 @@ cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream) {
   if (p.nsplit > 65535) return cudaErrorInvalidValue;
   dim3 grid(p.n_kv_heads, p.batch, p.nsplit);
   void* args[] = {const_cast<DecodeParams*>(&p)};
-  return cudaLaunchKernel(k.fn, grid, dim3(k.threads), args, k.smem, stream);
+  return launch_with_pdl(k.fn, grid, dim3(k.threads), args, k.smem, stream);
 }
 
 }  // namespace lara

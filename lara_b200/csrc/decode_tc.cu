@@ -241,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   unsigned* queue = reinterpret_cast<unsigned*>(p.status + 32);  // [0] ticket, [1] finished CTAs
 
+  allow_dependent_launch();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->full[s], 1);
@@ -273,6 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 8; ++i) pz[i] = make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
   }
+  // global memory (tickets, q, lengths, cache) only after the previous grid is done
+  grid_dependency_wait();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -348,6 +351,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&bars->full[st]);
       }
       bars->issued = ++n;
+      return true;
+    };
+    // Paged caches: the same as push(m, true), called by the whole warp; lane
+    // 0 keeps the ring, and when pages are shorter than a tile every lane
+    // issues one (page piece, K or V, 64-column half) box, so a tile costs one
+    // copy's issue latency instead of 4 x pieces copies in a row.
+    auto push_tile_warp = [&](const Meta& m) -> bool {
+      n = __shfl_sync(kFull, n, 0);
+      const int st = n % kStages;
+      int good = 1;
+      if (lane == 0) {
+        if (n >= kStages && !wait_or_abort(&bars->empty[st], ((n / kStages) - 1) & 1, abort))
+          good = 0;
+        else
+          metas[st] = m;
+      }
+      if (!__shfl_sync(kFull, good, 0)) return false;
+      uint8_t* ks = smem + kKOff + st * kKVBytes;
+      uint8_t* vs = smem + kVOff + st * kKVBytes;
+      const int bx = a.page_box;
+      const int ps_mask = (1 << p.page_log2) - 1;
+      if (bx == kTile) {
+        if (lane == 0) {
+          const int pg = page_at(m.tok0);
+          const int in_page = m.tok0 & ps_mask;
+          mbar_arrive_expect_tx(&bars->full[st], 2 * kKVBytes);
+          tma_load_4d_hint(ks, &tm_k, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+          tma_load_4d_hint(ks + kHalf, &tm_k, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+          tma_load_4d_hint(vs, &tm_v, 0, in_page, m.kvh, pg, &bars->full[st], pol);
+          tma_load_4d_hint(vs + kHalf, &tm_v, 64, in_page, m.kvh, pg, &bars->full[st], pol);
+        }
+      } else {
+        const int lg = p.page_log2;
+        const int pieces = min(kTile >> lg, (m.tok_end - m.tok0 + bx - 1) >> lg);
+        if (lane == 0) mbar_arrive_expect_tx(&bars->full[st], (uint32_t)pieces * 4u * (uint32_t)bx * 128u);
+        __syncwarp();
+        const int i = lane >> 2;  // page piece
+        if (i < pieces) {
+          const int idx = (m.tok0 >> lg) - pg0 + i;
+          const int pg = idx < kPageCache ? pcache[idx]
+                                          : page_uncached(bt_row, m.tok0 + (i << lg), lg, p.num_pages, p.status);
+          const int off = (i << lg) * 128 + ((lane & 1) ? kHalf : 0);
+          const CUtensorMap* tm = (lane & 2) ? &tm_v : &tm_k;
+          tma_load_4d_hint(((lane & 2) ? vs : ks) + off, tm, (lane & 1) * 64, 0, m.kvh, pg, &bars->full[st], pol);
+        }
+      }
+      ++n;
+      if (lane == 0) bars->issued = n;
       return true;
     };
     bool ok = true;
@@ -436,12 +487,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           m.qslot = qs;
           m.qpar = (qi >> 1) & 1;
           bars->q_issued = ++qi;
-          const int ntiles = (ntok + kTile - 1) / kTile;
-          for (int j = 0; ok && j < ntiles; ++j) {
-            m.tok0 = tok_begin + j * kTile;
-            m.flags = (j == 0 ? 1 : 0) | (j == ntiles - 1 ? 2 : 0);
-            ok = push(m, true);
+          if constexpr (!kPaged) {
+            const int ntiles = (ntok + kTile - 1) / kTile;
+            for (int j = 0; ok && j < ntiles; ++j) {
+              m.tok0 = tok_begin + j * kTile;
+              m.flags = (j == 0 ? 1 : 0) | (j == ntiles - 1 ? 2 : 0);
+              ok = push(m, true);
+            }
           }
+        }
+      }
+      if constexpr (kPaged) {
+        ok = __shfl_sync(kFull, ok, 0);
+        m.qslot = __shfl_sync(kFull, m.qslot, 0);
+        m.qpar = __shfl_sync(kFull, m.qpar, 0);
+        const int ntiles = (ntok + kTile - 1) / kTile;
+        for (int j = 0; ok && j < ntiles; ++j) {
+          m.tok0 = tok_begin + j * kTile;
+          m.flags = (j == 0 ? 1 : 0) | (j == ntiles - 1 ? 2 : 0);
+          ok = push_tile_warp(m);
         }
       }
       // lane 0 is done with this item's cache entries
@@ -901,7 +965,7 @@ cudaError_t decode_tc_launch(const DecodeParams& p, cudaStream_t stream) {
   const int sms = device_sm_count();
   const unsigned grid = (unsigned)(n_items < sms ? n_items : sms);
   void* args[] = {&mq, &mk, &mv, const_cast<DecodeParams*>(&p), &a};
-  return cudaLaunchKernel(fn, dim3(grid), dim3(kThreads), args, kSmemAlloc, stream);
+  return launch_with_pdl(fn, dim3(grid), dim3(kThreads), args, kSmemAlloc, stream);
 }
 
 }  // namespace lara

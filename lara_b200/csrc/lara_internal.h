@@ -96,12 +96,15 @@ int decode_tile_tokens(int head_dim, int group);
 // geometry only the tensor-core kernel runs (group 16); 0 = unsupported.
 int decode_chunk_granule(int head_dim, int group);
 
-// Tokens of the first split for a (nsplit, chunk) plan, or 0 for equal
-// splits.  With two splits the first covers 7/8 of the span: all first
-// chunks launch before any second chunk, so the short second chunks fill the
-// last wave (measured on B200: +1.2 to +3.8 % GB/s on 64 x 4096, 64 x 8192
-// and 96 x 4096 decodes).
-int decode_first_chunk(int nsplit, int chunk, int group, int head_dim);
+// Tokens of the first split for a (nsplit, chunk) plan over `units` (query
+// row, kv head) pairs, or 0 for equal splits.  With two splits the first
+// covers 7/8 of the span: all first chunks launch before any second chunk, so
+// the short second chunks fill the last wave (measured on B200: +1.2 to
+// +3.8 % GB/s on 64 x 4096, 64 x 8192 and 96 x 4096 decodes).  It applies
+// only when the first chunks alone occupy every SM: with fewer units, SMs
+// holding a long first chunk stream it alone while others finish early (8 x
+// 4096 ran at 0.26-0.35 of HBM, 16 x 4096 at 0.50-0.66).
+int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long units);
 
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream);
 
@@ -163,6 +166,12 @@ cudaError_t kv_append_paged_launch(uint16_t* k_pages, uint16_t* v_pages, const i
 cudaError_t pack_bf16_launch(const float* src, uint16_t* dst, size_t n, cudaStream_t stream);
 
 int device_sm_count();
+
+// Launch `fn` with programmatic stream serialization, so its CTAs may be
+// scheduled while the previous kernel in the stream finishes (the kernel must
+// call grid_dependency_wait() before touching global memory).  LARA_PDL=0
+// launches it the ordinary way.
+cudaError_t launch_with_pdl(const void* fn, dim3 grid, dim3 block, void** args, size_t smem, cudaStream_t stream);
 
 // Record the calling thread's last error message (lara_last_error_string)
 // and return `code`.

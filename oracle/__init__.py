@@ -15,6 +15,7 @@ were produced by importing the reference's own ``cpu_attention_numpy``
 from .attention import (  # noqa: F401
     PARITY_FLOOR_FRAC,
     PARITY_ULPS,
+    TC_SPLIT_P_KAPPA,
     bf16_parity_error,
     bf16_u16_to_fp32,
     bf16_ulp,

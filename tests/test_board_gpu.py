@@ -133,7 +133,7 @@ def test_driver_board_arithmetic(tmp_path):
         o_ieee = acc.run_attention(q, k, v, seq_len=64, causal=True, q_pos_base=31, kv_pos_base=7)
     np.testing.assert_array_equal(o, board.attention_board(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7))
     gold = oracle.cpu_attention_numpy(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
-    from parity import assert_bf16_parity
+    from parity import assert_bf16_parity, prefill_on_tensor_cores
 
     g64 = oracle.dense_attention_fp64(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
-    assert_bf16_parity(o_ieee, gold, g64, what="ieee after board")
+    assert_bf16_parity(o_ieee, gold, g64, what="ieee after board", tensor_core=prefill_on_tensor_cores(32, 8, 128))

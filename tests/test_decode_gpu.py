@@ -13,7 +13,7 @@ import pytest
 torch = pytest.importorskip("torch")
 
 import oracle  # noqa: E402
-from parity import assert_bf16_parity, words_of  # noqa: E402
+from parity import assert_bf16_parity, decode_on_tensor_cores, words_of  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -72,7 +72,7 @@ def test_decode_geometries_ragged(dev, geom):
     cap = 700
     lens = [cap, 1, 333, 64, 65][:B] if B <= 5 else [cap] * B
     o, gold, g64, _ = _run_case(dev, B, Hq, Hkv, D, lens, cap, seed=B * 100 + Hq)
-    assert_bf16_parity(o, gold, g64, what=str(geom))
+    assert_bf16_parity(o, gold, g64, what=str(geom), tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
 @pytest.mark.parametrize("splits", [(1, 4096), (4, 1024), (64, 64), (7, 640)])
@@ -81,7 +81,7 @@ def test_decode_forced_splits(dev, splits):
     B, Hq, Hkv, D, cap = 2, 32, 8, 128, 4096
     lens = [4096, 2999]
     o, gold, g64, _ = _run_case(dev, B, Hq, Hkv, D, lens, cap, seed=7, std=0.5, splits=splits)
-    assert_bf16_parity(o, gold, g64, what=f"splits={splits}")
+    assert_bf16_parity(o, gold, g64, what=f"splits={splits}", tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
 def test_decode_repeat_is_deterministic_and_counters_reset(dev):
@@ -105,13 +105,13 @@ def test_decode_repeat_is_deterministic_and_counters_reset(dev):
 def test_decode_zero_length_gives_zero(dev):
     o, gold, g64, _ = _run_case(dev, 3, 8, 2, 64, [0, 5, 0], 64, seed=11)
     assert not np.any(o[0]) and not np.any(o[2])
-    assert_bf16_parity(o[1:2], gold[1:2], g64[1:2])
+    assert_bf16_parity(o[1:2], gold[1:2], g64[1:2], tensor_core=decode_on_tensor_cores(8, 2, 64))
 
 
 def test_decode_large_logits_stress(dev):
     """Config-3 style: K channels 0..3 scaled by 20 (large logits)."""
     o, gold, g64, _ = _run_case(dev, 2, 64, 8, 128, [4100, 777], 4100, seed=2, boost=20.0)
-    assert_bf16_parity(o, gold, g64, what="large logits")
+    assert_bf16_parity(o, gold, g64, what="large logits", tensor_core=decode_on_tensor_cores(64, 8, 128))
 
 
 def test_decode_zero_inputs(dev):
@@ -297,7 +297,8 @@ def test_config3_ragged_sampled(dev):
         for h in hs:
             sl = slice(h * G, (h + 1) * G)
             assert_bf16_parity(o[b, sl], gold[0, sl], g64[0, sl],
-                               what=f"cfg3 b={b} len={n} kvh={h} max|logit|={peak[b]:.1f}")
+                               what=f"cfg3 b={b} len={n} kvh={h} max|logit|={peak[b]:.1f}",
+                               tensor_core=decode_on_tensor_cores(cfg.n_q_heads, Hkv, D))
 
 
 @pytest.mark.slow

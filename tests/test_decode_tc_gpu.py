@@ -19,7 +19,7 @@ import pytest
 torch = pytest.importorskip("torch")
 
 import oracle  # noqa: E402
-from parity import assert_bf16_parity, words_of  # noqa: E402
+from parity import assert_bf16_parity, decode_on_tensor_cores, words_of  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -106,14 +106,14 @@ def test_tc_geometries_ragged(tc, geom):
     cap = 700
     lens = [cap, 1, 333, 128, 129][:B]
     o, gold, g64, _ = _case(tc, B, Hq, Hkv, lens, cap, seed=B * 100 + Hq)
-    assert_bf16_parity(o, gold, g64, what=f"tc {geom}")
+    assert_bf16_parity(o, gold, g64, what=f"tc {geom}", tensor_core=decode_on_tensor_cores(Hq, Hkv, 128))
 
 
 @pytest.mark.parametrize("splits", [(1, 4096), (4, 1024), (64, 64), (7, 640), (3, 1376)])
 def test_tc_forced_splits(tc, splits):
     """Split partials and the last-arriver merge for several plans (G = 8)."""
     o, gold, g64, _ = _case(tc, 2, 64, 8, [4096, 2999], 4096, seed=7, std=0.5, splits=splits)
-    assert_bf16_parity(o, gold, g64, what=f"tc splits={splits}")
+    assert_bf16_parity(o, gold, g64, what=f"tc splits={splits}", tensor_core=decode_on_tensor_cores(64, 8, 128))
 
 
 def test_tc_many_items_per_cta(tc):
@@ -125,7 +125,8 @@ def test_tc_many_items_per_cta(tc):
     o, gold, g64, _ = _case(tc, 40, 64, 8, lens, 3000, seed=12, std=0.5, splits=(12, 256))
     assert not np.any(o[3])
     keep = [b for b in range(40) if lens[b] > 0]
-    assert_bf16_parity(o[keep], gold[keep], g64[keep], what="tc many items")
+    assert_bf16_parity(o[keep], gold[keep], g64[keep], what="tc many items",
+                       tensor_core=decode_on_tensor_cores(64, 8, 128))
 
 
 @pytest.mark.parametrize("path", ["tc", "simt"])
@@ -133,19 +134,19 @@ def test_poisoned_cache_tail(dev, monkeypatch, path):
     """NaN / Inf past each sequence's length (the unwritten part of a cache) is never read into the output."""
     monkeypatch.setenv("LARA_DECODE_PATH", path)
     o, gold, g64, _ = _case(dev, 4, 64, 8, [700, 5, 129, 256], 700, seed=21, poison=True)
-    assert_bf16_parity(o, gold, g64, what=f"{path} poisoned tail")
+    assert_bf16_parity(o, gold, g64, what=f"{path} poisoned tail", tensor_core=decode_on_tensor_cores(64, 8, 128))
 
 
 def test_tc_zero_length_gives_zero(tc):
     o, gold, g64, _ = _case(tc, 3, 64, 8, [0, 5, 0], 64, seed=11)
     assert not np.any(o[0]) and not np.any(o[2])
-    assert_bf16_parity(o[1:2], gold[1:2], g64[1:2])
+    assert_bf16_parity(o[1:2], gold[1:2], g64[1:2], tensor_core=decode_on_tensor_cores(64, 8, 128))
 
 
 def test_tc_large_logits(tc):
     """Config-3 style: K channels 0..3 scaled by 20 (large logits)."""
     o, gold, g64, _ = _case(tc, 2, 64, 8, [4100, 777], 4100, seed=2, boost=20.0)
-    assert_bf16_parity(o, gold, g64, what="tc large logits")
+    assert_bf16_parity(o, gold, g64, what="tc large logits", tensor_core=decode_on_tensor_cores(64, 8, 128))
 
 
 def test_tc_repeat_is_deterministic_and_queue_resets(tc):
@@ -195,7 +196,8 @@ def test_tc_partial_plus_lse_combine_equals_full(tc):
     o = ops.lse_combine(torch.stack(mls), torch.stack(accs)).view(B, Hq, D)
     kw, vw = words_of(k), words_of(v)
     gold = oracle.decode_attention(qw, kw, vw, np.full(B, L))
-    assert_bf16_parity(words_of(o), gold, oracle.decode_attention_fp64(qw, kw, vw, np.full(B, L)), what="tc combine")
+    assert_bf16_parity(words_of(o), gold, oracle.decode_attention_fp64(qw, kw, vw, np.full(B, L)), what="tc combine",
+                       tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
 @pytest.mark.parametrize("path", ["tc", "simt"])
@@ -231,8 +233,9 @@ def test_prefill_rows_on_decode_kernels(dev, monkeypatch, path):
             c = cached[b]
             args = (qw[b:b + 1].transpose(0, 2, 1, 3), kw[b:b + 1], vw[b:b + 1], np.array([c + n]), c)
             gold = oracle.prefill_attention(*args, causal=True)[0]
-            g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64)[0]
-            assert_bf16_parity(ow[b].transpose(1, 0, 2), gold, g64, what=f"{path} prefill rows b={b}")
+            g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64, kappa=True)[0]
+            assert_bf16_parity(ow[b].transpose(1, 0, 2), gold, g64, what=f"{path} prefill rows b={b}",
+                               tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
 @pytest.mark.parametrize("path", ["tc", "simt"])
@@ -251,7 +254,8 @@ def test_dense_transaction_on_decode_kernels(dev, monkeypatch, path):
     o = words_of(ops.attention_dense(t(q), t(k), t(v), causal=True, q_pos_base=31, kv_pos_base=7))
     geo = dict(causal=True, q_pos_base=31, kv_pos_base=7, n_q_heads=Hq, n_kv_heads=Hkv, head_dim=D)
     gold = oracle.cpu_attention_numpy(q, k, v, **geo)
-    assert_bf16_parity(o, gold, oracle.dense_attention_fp64(q, k, v, **geo), what=f"dense {path}")
+    assert_bf16_parity(o, gold, oracle.dense_attention_fp64(q, k, v, **geo), what=f"dense {path}",
+                       tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
 def _list_schedule_plan(lens, L, hkv, sms, overhead=1.0):
@@ -311,4 +315,5 @@ def test_tc_long_sequence_many_splits(tc):
     B, Hq, Hkv, L = 1, 64, 8, 300_000
     for splits in ((0, 0), (300, 1024)):
         o, gold, g64, dec = _case(tc, B, Hq, Hkv, [L], L, seed=31, std=0.5, splits=splits)
-        assert_bf16_parity(o, gold, g64, what=f"tc long sequence splits={splits} plan={dec.plan}")
+        assert_bf16_parity(o, gold, g64, what=f"tc long sequence splits={splits} plan={dec.plan}",
+                           tensor_core=decode_on_tensor_cores(Hq, Hkv, 128))

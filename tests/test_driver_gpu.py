@@ -19,7 +19,7 @@ torch = pytest.importorskip("torch")
 
 import make_golden as mg  # noqa: E402
 import oracle  # noqa: E402
-from parity import assert_bf16_parity, words_of  # noqa: E402
+from parity import assert_bf16_parity, decode_on_tensor_cores, prefill_on_tensor_cores, words_of  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -46,10 +46,11 @@ def test_board_case_matrix(accel, golden_dir, case):
     rows = fx["rows"]
     g64 = oracle.dense_attention_fp64(q, k, v, causal=causal, q_pos_base=qb, kv_pos_base=kb)
     # against the reference's own output rows
-    assert_bf16_parity(out[:, rows, :], fx["o_rows"], g64[:, rows, :], what=f"{name} vs reference rows")
+    tc = prefill_on_tensor_cores(32, 8, 128)
+    assert_bf16_parity(out[:, rows, :], fx["o_rows"], g64[:, rows, :], what=f"{name} vs reference rows", tensor_core=tc)
     # against the pinned oracle (full output) and fp64
     gold = oracle.cpu_attention_numpy(q, k, v, causal=causal, q_pos_base=qb, kv_pos_base=kb)
-    assert_bf16_parity(out, gold, g64, what=f"{name} vs oracle")
+    assert_bf16_parity(out, gold, g64, what=f"{name} vs oracle", tensor_core=tc)
     # harness invariants (sw/board_performance.py:345-378)
     perf = accel.read_perf()
     prof = accel.last_profile
@@ -108,8 +109,8 @@ def test_dead_causal_rows_are_zero(accel):
     assert not np.any(out[:, :8])
     args = (q[None], k[None], v[None], np.array([16]), 0)
     gold = oracle.prefill_attention(*args, causal=True, kv_pos_base=8)[0]
-    g64 = oracle.prefill_attention(*args, causal=True, kv_pos_base=8, dtype=np.float64)[0]
-    assert_bf16_parity(out[:, 8:], gold[:, 8:], g64[:, 8:])
+    g64 = oracle.prefill_attention(*args, causal=True, kv_pos_base=8, dtype=np.float64, kappa=True)[0]
+    assert_bf16_parity(out[:, 8:], gold[:, 8:], g64[:, 8:], tensor_core=prefill_on_tensor_cores(32, 8, 128))
 
 
 def test_closed_accelerator_raises():
@@ -140,7 +141,7 @@ def test_decode_extension_cfg1(golden_dir):
         k_all = np.concatenate([fx["k_cache"], fx["k_new"][:, :, None, :]], axis=2)
         v_all = np.concatenate([fx["v_cache"], fx["v_new"][:, :, None, :]], axis=2)
         g64 = oracle.decode_attention_fp64(fx["q"], k_all, v_all, np.array([513]))
-        assert_bf16_parity(o, fx["o_fp32"], g64, what="driver run_query cfg1")
+        assert_bf16_parity(o, fx["o_fp32"], g64, what="driver run_query cfg1", tensor_core=decode_on_tensor_cores(8, 2, 64))
         np.testing.assert_array_equal(a.read_output(), o)
         perf = a.read_perf()
         assert 0 <= perf["mac_cycles"] <= perf["cycles"]
@@ -161,7 +162,8 @@ def test_decode_extension_ragged_batch():
         a.load_kv(k, v, lens)
         o = a.run_query(q)
     gold = oracle.decode_attention(q, k, v, lens)
-    assert_bf16_parity(o, gold, oracle.decode_attention_fp64(q, k, v, lens), what="ragged run_query")
+    assert_bf16_parity(o, gold, oracle.decode_attention_fp64(q, k, v, lens), what="ragged run_query",
+                       tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
 def test_prefill_chunk_extension():
@@ -185,8 +187,9 @@ def test_prefill_chunk_extension():
         v_all = np.concatenate([v[b:b + 1, :, :c], vn[b:b + 1]], axis=2)
         args = (q[b:b + 1].transpose(0, 2, 1, 3), k_all, v_all, np.array([c + n]), c)
         gold = oracle.prefill_attention(*args, causal=True)
-        g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64)
-        assert_bf16_parity(o[b].transpose(1, 0, 2), gold[0], g64[0], what=f"prefill b={b}")
+        g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64, kappa=True)
+        assert_bf16_parity(o[b].transpose(1, 0, 2), gold[0], g64[0], what=f"prefill b={b}",
+                           tensor_core=prefill_on_tensor_cores(Hq, Hkv, D))
 
 
 def test_prefill_chunk_pinned_out_and_truncate_rewind():
@@ -234,8 +237,9 @@ def test_prefill_chunk_pinned_out_and_truncate_rewind():
         v_all = np.concatenate([v[b:b + 1, :, :c], vn[b:b + 1]], axis=2)
         args = (q[b:b + 1].transpose(0, 2, 1, 3), k_all, v_all, np.array([c + n]), c)
         gold = oracle.prefill_attention(*args, causal=True)
-        g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64)
-        assert_bf16_parity(o_page[b].transpose(1, 0, 2), gold[0], g64[0], what=f"pipelined prefill b={b}")
+        g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64, kappa=True)
+        assert_bf16_parity(o_page[b].transpose(1, 0, 2), gold[0], g64[0], what=f"pipelined prefill b={b}",
+                           tensor_core=prefill_on_tensor_cores(Hq, Hkv, D))
 
 
 def test_dense_ops_matches_driver(accel):
@@ -272,7 +276,8 @@ def test_run_query_pinned_host_buffers_match_pageable():
         assert 0 <= perf["mac_cycles"] <= perf["cycles"]
     lens = np.array([700, 1, 350])
     gold = oracle.decode_attention(q, k, v, lens)
-    assert_bf16_parity(o_pinned, gold, oracle.decode_attention_fp64(q, k, v, lens), what="pinned run_query")
+    assert_bf16_parity(o_pinned, gold, oracle.decode_attention_fp64(q, k, v, lens), what="pinned run_query",
+                       tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
 def test_run_layer_composes_prologue_and_attention():
@@ -346,7 +351,8 @@ def test_async_decode_and_prefill_match_synchronous_calls():
                 np.testing.assert_array_equal(got, want)
             else:
                 assert_bf16_parity(got, oracle.decode_attention(q, k, v, lens),
-                                   oracle.decode_attention_fp64(q, k, v, lens), what="lara_decode splits=3")
+                                   oracle.decode_attention_fp64(q, k, v, lens), what="lara_decode splits=3",
+                                   tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
         want_p = sync_acc.run_prefill_chunk(qp, kn, vn, causal=True)
         # keep the device inputs referenced until lara_sync: the call is asynchronous
         qpd, knd, vnd = t(qp), t(kn), t(vn)

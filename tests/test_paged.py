@@ -98,7 +98,7 @@ def test_paged_decode_equals_contiguous(monkeypatch, page_size, geom, path):
     torch = _torch()
     from lara_b200 import ops
     from lara_b200.paged import PagedKVCache
-    from parity import assert_bf16_parity, words_of
+    from parity import assert_bf16_parity, decode_on_tensor_cores, words_of
 
     D, G = geom
     if (path == "tc" and D != 128) or (path == "simt" and G > 8):
@@ -130,7 +130,8 @@ def test_paged_decode_equals_contiguous(monkeypatch, page_size, geom, path):
     np.testing.assert_array_equal(o_paged, o_contig)
     gold = oracle.decode_attention(q, k, v, np.array(lens))
     g64 = oracle.decode_attention_fp64(q, k, v, np.array(lens))
-    assert_bf16_parity(o_paged, gold, g64, what=f"paged ps={page_size} D={D} G={G}")
+    assert_bf16_parity(o_paged, gold, g64, what=f"paged ps={page_size} D={D} G={G}",
+                       tensor_core=decode_on_tensor_cores(hq, hkv, D))
     for i, s in enumerate(slots):  # every row landed where the table says
         ks, vs = cache.gather(s)
         np.testing.assert_array_equal(words_of(ks), k[i, :, :lens[i]])
@@ -201,7 +202,7 @@ def test_paged_chunk_past_the_page_cache(monkeypatch, path):
     torch = _torch()
     from lara_b200 import _native
     from lara_b200.ops import _stream, new_workspace, workspace_status
-    from parity import assert_bf16_parity, words_of
+    from parity import assert_bf16_parity, decode_on_tensor_cores, words_of
 
     monkeypatch.setenv("LARA_DECODE_PATH", path)
     lib = _native.lib
@@ -255,7 +256,8 @@ def test_paged_chunk_past_the_page_cache(monkeypatch, path):
     np.testing.assert_array_equal(o_paged, words_of(oc))
     gold = oracle.decode_attention(q, k, v, np.array(lens))
     g64 = oracle.decode_attention_fp64(q, k, v, np.array(lens))
-    assert_bf16_parity(o_paged, gold, g64, what=f"paged ps=16, 563 pages in one chunk ({path})")
+    assert_bf16_parity(o_paged, gold, g64, what=f"paged ps=16, 563 pages in one chunk ({path})",
+                       tensor_core=decode_on_tensor_cores(hq, hkv, D))
     tt[0, 540] = total + 5  # past both caches, inside the sequence
     paged()
     assert workspace_status(ws) & 0x8  # kDevBadPage

@@ -20,7 +20,7 @@ import pytest
 torch = pytest.importorskip("torch")
 
 import oracle  # noqa: E402
-from parity import assert_bf16_parity, words_of  # noqa: E402
+from parity import assert_bf16_parity, decode_on_tensor_cores, prefill_on_tensor_cores, words_of  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -79,8 +79,9 @@ def test_prefill_parity(monkeypatch, path, case):
         gold = oracle.prefill_attention(qw[b:b + 1].transpose(0, 2, 1, 3), kw[b:b + 1], vw[b:b + 1],
                                         np.array([c + n]), c, causal=causal)[0]
         g64 = oracle.prefill_attention(qw[b:b + 1].transpose(0, 2, 1, 3), kw[b:b + 1], vw[b:b + 1],
-                                       np.array([c + n]), c, causal=causal, dtype=np.float64)[0]
-        assert_bf16_parity(o[b].transpose(1, 0, 2), gold, g64, what=f"{path} b={b}")
+                                       np.array([c + n]), c, causal=causal, dtype=np.float64, kappa=True)[0]
+        assert_bf16_parity(o[b].transpose(1, 0, 2), gold, g64, what=f"{path} b={b}",
+                           tensor_core=prefill_on_tensor_cores(Hq, Hkv, D))
 
 
 @pytest.mark.parametrize("case", CASES[:5], ids=lambda c: "B{}_Hq{}_Hkv{}_c{}_n{}".format(
@@ -130,7 +131,8 @@ def test_dense_tc_matches_stream(monkeypatch):
     gold = oracle.cpu_attention_numpy(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
     g64 = oracle.dense_attention_fp64(q, k, v, causal=True, q_pos_base=31, kv_pos_base=7)
     for path, o in outs.items():
-        assert_bf16_parity(o, gold, g64, what=f"dense {path}")
+        assert_bf16_parity(o, gold, g64, what=f"dense {path}",
+                           tensor_core=path == "tc" or decode_on_tensor_cores(32, 8, 128))
 
 
 @pytest.mark.slow
@@ -183,8 +185,9 @@ def test_config5_full_size_sampled(monkeypatch):
             qs = qw[b:b + 1, i0:i0 + 2].transpose(0, 2, 1, 3)
             args = (qs, kw, vw, np.array([C + n]), C + i0)
             gold = oracle.prefill_attention(*args, causal=True)[0]
-            g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64)[0]
-            assert_bf16_parity(ow[b, i0:i0 + 2].transpose(1, 0, 2), gold, g64, what=f"cfg5 b={b} rows {i0}+2")
+            g64 = oracle.prefill_attention(*args, causal=True, dtype=np.float64, kappa=True)[0]
+            assert_bf16_parity(ow[b, i0:i0 + 2].transpose(1, 0, 2), gold, g64, what=f"cfg5 b={b} rows {i0}+2",
+                               tensor_core=prefill_on_tensor_cores(Hq, Hkv, D))
 
 
 def test_ops_gqa_prefill_matches_abi():
