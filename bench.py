@@ -692,7 +692,7 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
     import torch
 
     from lara_b200 import _native, ops
-    from lara_b200.workloads import PREFILL, prefill_shard, prefill_units
+    from lara_b200.workloads import PREFILL, prefill_launch_groups, prefill_shard, prefill_units
 
     cfg = PREFILL
     G, D, C, n = cfg.n_q_heads // cfg.n_kv_heads, cfg.head_dim, cfg.cached, cfg.new
@@ -701,11 +701,11 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
     lib = _native.lib
     pieces = prefill_units(cfg, world, rank)
     parts = []
-    for b, h0, nh in pieces:
-        q, k, v, kn, vn, lens0 = prefill_shard(cfg, dev, b, h0, nh)
-        nb = int(lib.lara_prefill_workspace_bytes(1, n, nh * G, nh, D, C + n))
+    for b, nseq, h0, nh in prefill_launch_groups(cfg, pieces):
+        q, k, v, kn, vn, lens0 = prefill_shard(cfg, dev, b, h0, nh, nseq)
+        wsb = int(lib.lara_prefill_workspace_bytes(nseq, n, nh * G, nh, D, C + n))
         rank_bytes = sum(t.numel() * 2 for t in (q, k, v, kn, vn)) + q.numel() * 2
-        parts.append({"b": b, "h0": h0, "nh": nh, "lens0": lens0, "ws": ops.new_workspace(nb, dev),
+        parts.append({"b": b, "nb": nseq, "h0": h0, "nh": nh, "lens0": lens0, "ws": ops.new_workspace(wsb, dev),
                       "bytes": rank_bytes,
                       "copies": [{"q": q, "k": k, "v": v, "kn": kn, "vn": vn, "o": torch.empty_like(q),
                                   "lens": lens0.clone()}]})
@@ -715,11 +715,11 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
         for _ in range(R - 1):
             p["copies"].append({key: t.clone() for key, t in c0.items()})
     pairs_per_head = n * C + n * (n + 1) // 2
-    flops = sum(p["nh"] * G * pairs_per_head * 4 * D for p in parts)
+    flops = sum(p["nb"] * p["nh"] * G * pairs_per_head * 4 * D for p in parts)
 
     def attend(p, c):
         _native.check(lib.lara_gqa_prefill(c["q"].data_ptr(), c["k"].data_ptr(), c["v"].data_ptr(),
-                                           p["lens0"].data_ptr(), c["o"].data_ptr(), 1, n, p["nh"] * G, p["nh"], D,
+                                           p["lens0"].data_ptr(), c["o"].data_ptr(), p["nb"], n, p["nh"] * G, p["nh"], D,
                                            C + n, 1, scale, p["ws"].data_ptr(), p["ws"].numel(),
                                            stream.cuda_stream), "prefill")
 
@@ -761,10 +761,10 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
         if not (np.array_equal(kw_all[:, :, C:], _words(c["kn"])) and np.array_equal(vw_all[:, :, C:],
                                                                                      _words(c["vn"]))):
             tally.r["finite"] = False  # the append did not land where it should
-        qw, ow = _words(c["q"]), _words(c["o"])
+        qw, ow = _words(c["q"][:1]), _words(c["o"][:1])
         for i0 in (127, n - 2):
             qs = qw[:, i0:i0 + 2].transpose(0, 2, 1, 3)
-            args_ = (qs, kw_all, vw_all, np.array([C + n]), C + i0)
+            args_ = (qs, kw_all[:1], vw_all[:1], np.array([C + n]), C + i0)
             gold = oracle.prefill_attention(*args_, causal=True)[0]
             g64 = oracle.prefill_attention(*args_, causal=True, dtype=np.float64, kappa=True)[0]
             tally.add(ow[0, i0:i0 + 2].transpose(1, 0, 2), gold, g64, os.environ.get("LARA_ATTN_PATH") != "stream")
@@ -780,9 +780,10 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
         "steps": steps, "warmup": warmup, "scaling": "strong",
         "gpu_launches": steps * 3 * len(parts),
         "run": {"parallelism": f"(sequence, kv head) units split x{world}: rank {rank} holds "
-                               f"{[(b, f'kv {h0}..{h0 + nh - 1}') for b, h0, nh in pieces]}",
-                "step": "length reset + K/V append + attention (3 kernels per piece: append, length update, "
-                        "prefill)",
+                               f"{[(b, f'kv {h0}..{h0 + nh - 1}') for b, h0, nh in pieces]}, "
+                               f"{len(parts)} launch group(s)",
+                "step": "length reset + K/V append + attention (3 kernels per launch group: append, length "
+                        "update, prefill)",
                 "p_precision": "bf16 RNE (LARA_TC_SPLIT_P=0)" if os.environ.get("LARA_TC_SPLIT_P") == "0"
                 else "P_hi + P_lo", "input_copies": R,
                 "l2": f"{R} copies of the rank's inputs rotated (>= 4x L2 between re-reads)" if R > 1
@@ -826,15 +827,15 @@ def _prefill_e2e(args, cfg, parts, comm, dev) -> dict:
             oh, on = pinned(torch.empty_like(c["q"]))
             acc = AttentionAccelerator(device=dev.index)
             accs.append(acc)
-            acc.configure_heads(p["nh"] * G, p["nh"], D, max_seq_len=C + n, batch=1)
-            acc.load_kv(_words(c["k"][:, :, :C]), _words(c["v"][:, :, :C]), np.array([C], np.int32))
-            jobs.append((acc, qn, knn, vnn, on, c["o"]))
+            acc.configure_heads(p["nh"] * G, p["nh"], D, max_seq_len=C + n, batch=p["nb"])
+            acc.load_kv(_words(c["k"][:, :, :C]), _words(c["v"][:, :, :C]), np.full(p["nb"], C, np.int32))
+            jobs.append((acc, qn, knn, vnn, on, c["o"], p["nb"]))
             h2d += sum(x.numel() * 2 for x in (qh, knh, vnh))
             d2h += oh.numel() * 2
 
         def e2e_step():
-            for acc, qn, knn, vnn, on, _ in jobs:
-                acc.truncate_kv(np.array([C], np.int32))
+            for acc, qn, knn, vnn, on, _, nseq in jobs:
+                acc.truncate_kv(np.full(nseq, C, np.int32))
                 acc.run_prefill_chunk(qn, knn, vnn, causal=True, out=on)
         for _ in range(2):
             e2e_step()
@@ -845,7 +846,7 @@ def _prefill_e2e(args, cfg, parts, comm, dev) -> dict:
             e2e_step()
         ms = (time.perf_counter() - t0) * 1e3 / n_e2e
         comm.barrier()
-        for acc, qn, knn, vnn, on, o_dev in jobs:
+        for acc, qn, knn, vnn, on, o_dev, _ in jobs:
             if not np.array_equal(on, _words(o_dev)):
                 raise RuntimeError("API output differs from the timed kernel output")
     finally:

@@ -727,7 +727,8 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
     const long long sms = device_sm_count();
     if (uniform) {
       const int len0 = lens_host ? (lens_host[0] < 1 ? 1 : lens_host[0]) : L;
-      const long long ctas = (long long)batch * n_kv_heads * ((len0 + chunk - 1) / chunk);
+      const long long units = (long long)batch * n_kv_heads;
+      const long long ctas = units * ((len0 + chunk - 1) / chunk);
       const long long per_sm = (ctas + sms - 1) / sms;
       const int per = len0 < chunk ? len0 : chunk;
       // An SM that only ever holds one CTA streams at about 70% of the rate
@@ -735,6 +736,15 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
       // with more CTAs per SM the neighbour hides each one's prologue.
       const double lone = (cps > 1 && per_sm == 1) ? 1.0 / 0.7 : 1.0;
       cost = (double)per_sm * (per + ovh) * lone;
+      const int c0 = decode_first_chunk(s_eff, chunk, group, head_dim, units);
+      if (c0 > 0 && len0 > chunk) {
+        // Long first chunks, launched first, cover every SM; the short second
+        // chunks then fill whichever SM frees a slot, so the busiest SM holds
+        // its share of first chunks or the average load plus one short chunk.
+        const double first = (double)((units + sms - 1) / sms) * (c0 + ovh);
+        const double fill = (double)units * len0 / sms + (len0 - c0) + 2 * ovh;
+        cost = first > fill ? first : fill;
+      }
     } else {
       long long ctas = 0;
       for (int b = 0; b < batch; ++b) ctas += (lens_host[b] + chunk - 1) / chunk;

@@ -260,25 +260,44 @@ def prefill_units(cfg: PrefillConfig, world: int, rank: int):
     return pieces
 
 
-def prefill_shard(cfg: PrefillConfig, device, b: int, h0: int, nh: int):
-    """Chunked-prefill inputs of kv heads [h0, h0+nh) of sequence b (and their
-    query heads): q [1, n, nh*G, D], cache k/v [1, nh, C+n, D] with the first C
-    tokens drawn, new k/v [1, nh, n, D], cached length [C].  Each (sequence,
-    tensor) is one generator stream over all heads, sliced to the rank's heads."""
+def prefill_launch_groups(cfg: PrefillConfig, pieces):
+    """Pieces grouped for launching: consecutive whole sequences (all kv heads)
+    form one batched group [(first sequence, sequences, 0, Hkv)]; a partial
+    sequence is a group of its own [(sequence, 1, first kv head, kv heads)]."""
+    groups = []
+    for b, h0, nh in pieces:
+        whole = h0 == 0 and nh == cfg.n_kv_heads
+        if whole and groups and groups[-1][2] == 0 and groups[-1][3] == cfg.n_kv_heads \
+                and groups[-1][0] + groups[-1][1] == b:
+            groups[-1] = (groups[-1][0], groups[-1][1] + 1, 0, nh)
+        else:
+            groups.append((b, 1, h0, nh))
+    return groups
+
+
+def prefill_shard(cfg: PrefillConfig, device, b: int, h0: int, nh: int, nb: int = 1):
+    """Chunked-prefill inputs of kv heads [h0, h0+nh) of sequences [b, b+nb)
+    (and their query heads): q [nb, n, nh*G, D], cache k/v [nb, nh, C+n, D]
+    with the first C tokens drawn, new k/v [nb, nh, n, D], cached lengths [C]*nb.
+    Each (sequence, tensor) is one generator stream over all heads, sliced to
+    the requested heads."""
     import torch
 
     dev = torch.device(device)
     G, D, C, n = cfg.n_q_heads // cfg.n_kv_heads, cfg.head_dim, cfg.cached, cfg.new
     Hq, Hkv = cfg.n_q_heads, cfg.n_kv_heads
-
-    def draw(kind, shape):
-        return torch.randn(shape, generator=_generator(dev, cfg.seed, kind, b), device=dev) * cfg.std
-
-    q = draw(_Q, (n, Hq, D))[:, h0 * G:(h0 + nh) * G].to(torch.bfloat16).unsqueeze(0).contiguous()
-    k = torch.zeros((1, nh, C + n, D), dtype=torch.bfloat16, device=dev)
+    q = torch.empty((nb, n, nh * G, D), dtype=torch.bfloat16, device=dev)
+    k = torch.zeros((nb, nh, C + n, D), dtype=torch.bfloat16, device=dev)
     v = torch.zeros_like(k)
-    k[0, :, :C] = draw(_K, (Hkv, C, D))[h0:h0 + nh].to(torch.bfloat16)
-    v[0, :, :C] = draw(_V, (Hkv, C, D))[h0:h0 + nh].to(torch.bfloat16)
-    kn = draw(_KNEW, (Hkv, n, D))[h0:h0 + nh].to(torch.bfloat16).unsqueeze(0).contiguous()
-    vn = draw(_VNEW, (Hkv, n, D))[h0:h0 + nh].to(torch.bfloat16).unsqueeze(0).contiguous()
-    return q, k, v, kn, vn, torch.tensor([C], dtype=torch.int32, device=dev)
+    kn = torch.empty((nb, nh, n, D), dtype=torch.bfloat16, device=dev)
+    vn = torch.empty_like(kn)
+    for i in range(nb):
+        def draw(kind, shape):
+            return torch.randn(shape, generator=_generator(dev, cfg.seed, kind, b + i), device=dev) * cfg.std
+
+        q[i] = draw(_Q, (n, Hq, D))[:, h0 * G:(h0 + nh) * G].to(torch.bfloat16)
+        k[i, :, :C] = draw(_K, (Hkv, C, D))[h0:h0 + nh].to(torch.bfloat16)
+        v[i, :, :C] = draw(_V, (Hkv, C, D))[h0:h0 + nh].to(torch.bfloat16)
+        kn[i] = draw(_KNEW, (Hkv, n, D))[h0:h0 + nh].to(torch.bfloat16)
+        vn[i] = draw(_VNEW, (Hkv, n, D))[h0:h0 + nh].to(torch.bfloat16)
+    return q, k, v, kn, vn, torch.full((nb,), C, dtype=torch.int32, device=dev)

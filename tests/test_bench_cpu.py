@@ -90,7 +90,7 @@ def test_rotation_count_covers_four_l2():
 
 
 def test_prefill_units_partition_every_unit_once():
-    from lara_b200.workloads import PREFILL, prefill_units
+    from lara_b200.workloads import PREFILL, prefill_launch_groups, prefill_units
 
     for world in range(1, 9):
         seen = []
@@ -99,6 +99,10 @@ def test_prefill_units_partition_every_unit_once():
                 assert 0 <= h0 and h0 + nh <= PREFILL.n_kv_heads and nh > 0
                 seen += [(b, h) for h in range(h0, h0 + nh)]
         assert sorted(seen) == [(b, h) for b in range(PREFILL.batch) for h in range(PREFILL.n_kv_heads)]
+    # whole sequences of a rank share one batched launch; a split sequence is a launch of its own
+    assert prefill_launch_groups(PREFILL, prefill_units(PREFILL, 1, 0)) == [(0, 4, 0, 8)]
+    assert prefill_launch_groups(PREFILL, prefill_units(PREFILL, 8, 3)) == [(1, 1, 4, 4)]
+    assert prefill_launch_groups(PREFILL, prefill_units(PREFILL, 3, 1)) == [(1, 1, 3, 5), (2, 1, 0, 6)]
 
 
 def test_decode_shard_is_rank_independent(monkeypatch):
