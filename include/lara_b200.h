@@ -83,13 +83,7 @@ LARA_API int lara_device_query(int device, lara_device_info* out);
 
 /* Split plan for a decode workload on the current device.  lens_host may be
  * NULL (every sequence is max_seq_len long) or point to B host int32 lengths.
- * Writes the split count (grid.x) and tokens per split.  A negative
- * chunk_tokens is a balanced plan, chosen for uniform batches too small to
- * fill the SMs evenly with whole splits: the (sequence, kv head) units' tokens
- * are laid end to end and cut into runs of -chunk_tokens tokens, one per CTA,
- * and num_splits is the partial slots a unit may need (the workspace size).
- * Pass the plan unchanged to the decode entry points; on a paged cache or the
- * tensor-core kernel it runs as equal splits of -chunk_tokens tokens. */
+ * Writes the split count (grid.x) and tokens per split. */
 LARA_API int lara_decode_plan(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len,
                      const int32_t* lens_host, int* num_splits, int* chunk_tokens);
 
@@ -121,8 +115,7 @@ LARA_API int lara_workspace_status(void* workspace, void* stream, int* device_st
  * bf16 in, exact products, fp32 accumulation and online softmax, bf16 RNE out.
  * seq_lens: device int32[B], each in [0, max_seq_len]; a sequence of length 0
  * gives a zero output.  num_splits/chunk_tokens come from lara_decode_plan
- * (num_splits * chunk_tokens >= max_seq_len, or a balanced plan with
- * chunk_tokens < 0); pass 0/0 to plan here.
+ * (num_splits * chunk_tokens >= max_seq_len); pass 0/0 to plan here.
  * Replaces: AttentionAccelerator.run_attention (sw/attn_driver.py:469-550)
  * and the datapath it drives (hw/rtl/attn_top.sv:301-625) for one query token
  * per sequence over a resident cache. */

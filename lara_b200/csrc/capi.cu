@@ -73,19 +73,6 @@ struct DeviceGuard {
 };
 
 int resolve_plan(int batch, int hq, int hkv, int d, int lmax, const int32_t* lens_host, int* nsplit, int* chunk) {
-  if (*nsplit > 0 && *chunk < 0) {
-    // a balanced plan (lara_decode_plan may return one): -chunk tokens per CTA
-    const int tile = lara::balanced_tile_tokens(d, hq / hkv);
-    if (tile <= 0 || (-*chunk) % tile != 0)
-      return fail(LARA_ERR_BAD_CFG, "balanced chunk_tokens (%d) needs a multiple of the kernel tile (%d)", -*chunk,
-                  tile);
-    const int slots = lara::balanced_partial_slots(lmax, -*chunk, d, hq / hkv);
-    if (slots == 0)
-      return fail(LARA_ERR_BAD_CFG, "balanced chunk_tokens (%d) spans more sequences than a CTA tracks", -*chunk);
-    if (*nsplit < slots)
-      return fail(LARA_ERR_BAD_CFG, "balanced plan with %d tokens per CTA needs num_splits >= %d", -*chunk, slots);
-    return LARA_OK;
-  }
   if (*nsplit > 0 && *chunk > 0) {
     const int tile = lara::decode_chunk_granule(d, hq / hkv);
     if (*chunk % tile != 0)
@@ -95,7 +82,7 @@ int resolve_plan(int batch, int hq, int hkv, int d, int lmax, const int32_t* len
                   (long long)*nsplit * *chunk, lmax);
     return LARA_OK;
   }
-  lara::decode_plan(batch, hkv, hq, d, lmax, lens_host, nsplit, chunk, true);
+  lara::decode_plan(batch, hkv, hq, d, lmax, lens_host, nsplit, chunk);
   return LARA_OK;
 }
 
@@ -354,7 +341,7 @@ int lara_decode_plan(int batch, int n_q_heads, int n_kv_heads, int head_dim, int
   int rc = check_geometry(batch, n_q_heads, n_kv_heads, head_dim, max_seq_len);
   if (rc) return rc;
   if (!num_splits || !chunk_tokens) return fail(LARA_ERR_STREAM_DEST, "null output pointer");
-  lara::decode_plan(batch, n_kv_heads, n_q_heads, head_dim, max_seq_len, lens_host, num_splits, chunk_tokens, true);
+  lara::decode_plan(batch, n_kv_heads, n_q_heads, head_dim, max_seq_len, lens_host, num_splits, chunk_tokens);
   return LARA_OK;
 }
 

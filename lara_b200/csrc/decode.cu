@@ -220,131 +220,6 @@ __device__ __forceinline__ void issue_tile_paged_warp(uint8_t* smem, uint64_t* f
   }
 }
 
-// One tile of K/V rows in shared memory through one warp's token slice
-// (rows Kt/Vt, the first `nvalid` of them valid): QK^T partial dot products,
-// the reduce-scatter that leaves one finished score per lane, the online
-// softmax update (running max / sum in the log2 domain, true exp2f) and P.V
-// into the register accumulator.  `pb` / `cb` are this warp's shared-memory
-// slots for the tile's probabilities and per-head rescale factors.  Shared by
-// the per-split and the balanced decode kernels.
-template <int D, int G>
-__device__ __forceinline__ void decode_tile(const uint8_t* Kt, const uint8_t* Vt, int nvalid, float scale_log2,
-                                            const float2 (&qp)[G][Traits<D, G>::kVec / 2],
-                                            float2 (&acc)[G][Traits<D, G>::kVec / 2], float& m_run, float& l_run,
-                                            float* pb, float* cb, int half, int c, int xperm, int my_tw, int my_g,
-                                            bool dup_writer, bool head_writer) {
-  using T = Traits<D, G>;
-  constexpr int V = T::kVec;
-  constexpr int V2 = V / 2;
-
-  // QK^T: ITER token rows x G heads of partial dot products over V dims,
-  // accumulated as (even, odd) dim pairs with packed fp32 FMA.  Slot
-  // it * G + g holds pass it ^ xperm of head g (see the reduce-scatter).
-  float part[T::kNV];
-#pragma unroll
-  for (int it = 0; it < T::kIter; ++it) {
-    const int tw = (it ^ xperm) * T::kTPI + half;
-    float2 kp[V2];
-    load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Kt + tw * T::kRowBytes) + c * V, kp);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float2 a2 = __fmul2_rn(qp[g][0], kp[0]);
-#pragma unroll
-      for (int j = 1; j < V2; ++j) a2 = __ffma2_rn(qp[g][j], kp[j], a2);
-      part[it * G + g] = a2.x + a2.y;
-    }
-  }
-  // Reduce-scatter over the row's lanes: each step halves the values a lane
-  // keeps and adds the partner's matching half.  Each step's half boundary
-  // is a bit of the pass index (first kHP steps) or of the head index; every
-  // lane took its passes in the order it ^ xperm and holds head g ^ yperm in
-  // slot g, so the half it keeps is always in its low slots and it simply
-  // sends the high slots.
-#pragma unroll
-  for (int step = 0; step < T::kH; ++step) {
-    const int off = T::kLPT >> (step + 1);
-    const int nv = T::kNV >> step;
-    // two kept values per packed FADD2 (the same two round-to-nearest sums)
-#pragma unroll
-    for (int j = 0; j + 1 < nv / 2; j += 2) {
-      const float2 mine = make_float2(part[j], part[j + 1]);
-      const float2 theirs = make_float2(__shfl_xor_sync(0xffffffffu, part[j + nv / 2], off),
-                                        __shfl_xor_sync(0xffffffffu, part[j + 1 + nv / 2], off));
-      const float2 sum = __fadd2_rn(mine, theirs);
-      part[j] = sum.x;
-      part[j + 1] = sum.y;
-    }
-    if ((nv / 2) & 1) part[nv / 2 - 1] += __shfl_xor_sync(0xffffffffu, part[nv - 1], off);
-  }
-#pragma unroll
-  for (int step = 0; step < T::kR; ++step) {
-    const int off = (T::kLPT >> T::kH) >> (step + 1);
-    part[0] += __shfl_xor_sync(0xffffffffu, part[0], off);
-  }
-  const float s = (my_tw < nvalid) ? part[0] * scale_log2 : -INFINITY;
-
-  // Online softmax for this lane's head over the warp's token slice.
-  float tmax = s;
-#pragma unroll
-  for (int off = 1 << (T::kR + T::kLogG); off < 32; off <<= 1)
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-  const float m_new = fmaxf(m_run, tmax);
-  const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-  const float corr = exp2f(m_run - m_use);
-  const float pr = exp2f(s - m_use);
-  float tsum = pr;
-#pragma unroll
-  for (int off = 1 << (T::kR + T::kLogG); off < 32; off <<= 1)
-    tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
-  l_run = l_run * corr + tsum;
-  // The accumulator needs rescaling only if some head's running max moved.
-  const bool moved = __any_sync(0xffffffffu, m_new != m_run);
-  m_run = m_new;
-
-  if (dup_writer) pb[my_tw * G + my_g] = pr;
-  if (head_writer) cb[my_g] = corr;
-  __syncwarp();
-
-  // P.V with the rescale of the running accumulator.
-  if (moved) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float cr = cb[g];
-      const float2 cr2 = make_float2(cr, cr);
-#pragma unroll
-      for (int j = 0; j < V2; ++j) acc[g][j] = __fmul2_rn(acc[g][j], cr2);
-    }
-  }
-#pragma unroll
-  for (int it = 0; it < T::kIter; ++it) {
-    const int tw = it * T::kTPI + half;
-    if (tw < nvalid) {
-      float2 vp[V2];
-      load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Vt + tw * T::kRowBytes) + c * V, vp);
-      float pg[G];
-      const float* prow = pb + tw * G;
-      if constexpr (G % 4 == 0) {
-#pragma unroll
-        for (int g = 0; g < G; g += 4) {
-          const float4 f = *reinterpret_cast<const float4*>(prow + g);
-          pg[g] = f.x; pg[g + 1] = f.y; pg[g + 2] = f.z; pg[g + 3] = f.w;
-        }
-      } else if constexpr (G == 2) {
-        const float2 f = *reinterpret_cast<const float2*>(prow);
-        pg[0] = f.x; pg[1] = f.y;
-      } else {
-        pg[0] = prow[0];
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float2 p2 = make_float2(pg[g], pg[g]);
-#pragma unroll
-        for (int j = 0; j < V2; ++j) acc[g][j] = __ffma2_rn(p2, vp[j], acc[g][j]);
-      }
-    }
-  }
-}
-
 // kPaged: K/V in a page pool addressed through the block table; each cache
 // layout gets its own instantiation, so a kernel holds only the copy code it runs.
 template <int D, int G, bool kPaged>
@@ -494,9 +369,115 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     const uint8_t* Kt = smem + st * T::kStageBytes + warp * T::kTokPerWarp * T::kRowBytes;
     const uint8_t* Vt = Kt + T::kHalfStage;
     const int nvalid = min(T::kTile, ntok - i * T::kTile) - warp * T::kTokPerWarp;
-    decode_tile<D, G>(Kt, Vt, nvalid, p.scale_log2, qp, acc, m_run, l_run,
-                      pbuf + ((i & 1) * T::kWarps + warp) * (T::kTokPerWarp * G),
-                      cbuf + ((i & 1) * T::kWarps + warp) * G, half, c, xperm, my_tw, my_g, dup_writer, head_writer);
+
+    // QK^T: ITER token rows x G heads of partial dot products over V dims,
+    // accumulated as (even, odd) dim pairs with packed fp32 FMA.  Slot
+    // it * G + g holds pass it ^ xperm of head g (see the reduce-scatter).
+    float part[T::kNV];
+#pragma unroll
+    for (int it = 0; it < T::kIter; ++it) {
+      const int tw = (it ^ xperm) * T::kTPI + half;
+      float2 kp[V2];
+      load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Kt + tw * T::kRowBytes) + c * V, kp);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float2 a2 = __fmul2_rn(qp[g][0], kp[0]);
+#pragma unroll
+        for (int j = 1; j < V2; ++j) a2 = __ffma2_rn(qp[g][j], kp[j], a2);
+        part[it * G + g] = a2.x + a2.y;
+      }
+    }
+    // Reduce-scatter over the row's lanes: each step halves the values a lane
+    // keeps and adds the partner's matching half.  Each step's half boundary
+    // is a bit of the pass index (first kHP steps) or of the head index; every
+    // lane took its passes in the order it ^ xperm and holds head g ^ yperm in
+    // slot g, so the half it keeps is always in its low slots and it simply
+    // sends the high slots.
+#pragma unroll
+    for (int step = 0; step < T::kH; ++step) {
+      const int off = T::kLPT >> (step + 1);
+      const int nv = T::kNV >> step;
+      // two kept values per packed FADD2 (the same two round-to-nearest sums)
+#pragma unroll
+      for (int j = 0; j + 1 < nv / 2; j += 2) {
+        const float2 mine = make_float2(part[j], part[j + 1]);
+        const float2 theirs = make_float2(__shfl_xor_sync(0xffffffffu, part[j + nv / 2], off),
+                                          __shfl_xor_sync(0xffffffffu, part[j + 1 + nv / 2], off));
+        const float2 sum = __fadd2_rn(mine, theirs);
+        part[j] = sum.x;
+        part[j + 1] = sum.y;
+      }
+      if ((nv / 2) & 1) part[nv / 2 - 1] += __shfl_xor_sync(0xffffffffu, part[nv - 1], off);
+    }
+#pragma unroll
+    for (int step = 0; step < T::kR; ++step) {
+      const int off = (T::kLPT >> T::kH) >> (step + 1);
+      part[0] += __shfl_xor_sync(0xffffffffu, part[0], off);
+    }
+    const float s = (my_tw < nvalid) ? part[0] * p.scale_log2 : -INFINITY;
+
+    // Online softmax for this lane's head over the warp's token slice.
+    float tmax = s;
+#pragma unroll
+    for (int off = 1 << (T::kR + T::kLogG); off < 32; off <<= 1)
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+    const float m_new = fmaxf(m_run, tmax);
+    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+    const float corr = exp2f(m_run - m_use);
+    const float pr = exp2f(s - m_use);
+    float tsum = pr;
+#pragma unroll
+    for (int off = 1 << (T::kR + T::kLogG); off < 32; off <<= 1)
+      tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
+    l_run = l_run * corr + tsum;
+    // The accumulator needs rescaling only if some head's running max moved.
+    const bool moved = __any_sync(0xffffffffu, m_new != m_run);
+    m_run = m_new;
+
+    float* pb = pbuf + ((i & 1) * T::kWarps + warp) * (T::kTokPerWarp * G);
+    float* cb = cbuf + ((i & 1) * T::kWarps + warp) * G;
+    if (dup_writer) pb[my_tw * G + my_g] = pr;
+    if (head_writer) cb[my_g] = corr;
+    __syncwarp();
+
+    // P.V with the rescale of the running accumulator.
+    if (moved) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float cr = cb[g];
+        const float2 cr2 = make_float2(cr, cr);
+#pragma unroll
+        for (int j = 0; j < V2; ++j) acc[g][j] = __fmul2_rn(acc[g][j], cr2);
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < T::kIter; ++it) {
+      const int tw = it * T::kTPI + half;
+      if (tw < nvalid) {
+        float2 vp[V2];
+        load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Vt + tw * T::kRowBytes) + c * V, vp);
+        float pg[G];
+        const float* prow = pb + tw * G;
+        if constexpr (G % 4 == 0) {
+#pragma unroll
+          for (int g = 0; g < G; g += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(prow + g);
+            pg[g] = f.x; pg[g + 1] = f.y; pg[g + 2] = f.z; pg[g + 3] = f.w;
+          }
+        } else if constexpr (G == 2) {
+          const float2 f = *reinterpret_cast<const float2*>(prow);
+          pg[0] = f.x; pg[1] = f.y;
+        } else {
+          pg[0] = prow[0];
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float2 p2 = make_float2(pg[g], pg[g]);
+#pragma unroll
+          for (int j = 0; j < V2; ++j) acc[g][j] = __ffma2_rn(p2, vp[j], acc[g][j]);
+        }
+      }
+    }
     // Release the stage (mbarrier arrive: release semantics).  A warp that
     // then observes the release complete (test_wait: acquire) claims the
     // refill of tile i + kStages with one CAS; nobody blocks on it.
@@ -619,310 +600,6 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
 }
 
 // ---------------------------------------------------------------------------
-// Balanced schedule (contiguous caches).  The per-split kernel above gives
-// every CTA one (row, kv head, split); with fewer units than SM slots that
-// leaves some SMs two CTAs and others one, and the decode is limited by each
-// SM's issue rate, so the busiest SM sets the step time (batch 8 of
-// Llama-3-8B: 1 MB on 108 SMs, 0.5 MB on 40).  Here the units' tiles are laid
-// end to end, unit after unit, and cut into equal runs of `per` tiles, one run
-// per CTA: every SM streams the same bytes.  A run may end one unit and start
-// the next, so a CTA works through up to kMaxSeg segments; each segment
-// finishes like a split of the per-split kernel (its partial state, or the
-// output when one CTA holds the whole unit) and the last segment of a unit to
-// finish merges them.  The ring keeps prefetching across segment boundaries,
-// so the warps' merge uses its own shared-memory area, half a head vector at
-// a time.
-// ---------------------------------------------------------------------------
-
-constexpr int kBalMaxSeg = 8;  // segments (units touched) per CTA of the balanced kernel
-
-struct BalSeg {
-  int row, kvh, seq;
-  int tok_begin, ntok;     // token range of the unit this segment covers
-  int tile_first, ntiles;  // position of its tiles in the CTA's tile sequence
-  int nseg, slot;          // segments of the unit over all CTAs, and this one's partial slot
-  int pad[3];
-};
-static_assert(sizeof(BalSeg) == 48, "segment record");
-
-template <int D, int G>
-struct BalTraits {
-  using T = Traits<D, G>;
-  static constexpr int kMaxSeg = kBalMaxSeg;
-  static constexpr int kHalfD = D / 2;
-  static constexpr int kMergeOff = T::kPageOff;  // the page-block cache is unused for contiguous caches
-  static constexpr int kMergeFloats = T::kWarps * G * kHalfD + 2 * T::kWarps * G;
-  static constexpr int kSegOff = (kMergeOff + kMergeFloats * 4 + 15) / 16 * 16;
-  static constexpr int kMetaOff = kSegOff + kMaxSeg * (int)sizeof(BalSeg);  // [0] segments, [1] tiles
-  static constexpr int kSmemBytes = kMetaOff + 16;
-  // two CTAs per SM, as for the per-split kernel (228 KB per SM, 1 KB reserved per CTA)
-  static constexpr bool kFits = 2 * (kSmemBytes + 1024) <= 233472;
-};
-
-// Issue tile t of the CTA's tile sequence (K rows then V rows) into its stage.
-template <int D, int G>
-__device__ __forceinline__ void issue_tile_balanced(uint8_t* smem, uint64_t* full, int t, const BalSeg* segs,
-                                                    int nsegs, const DecodeParams& p, uint64_t pol) {
-  using T = Traits<D, G>;
-  int s = 0;
-  while (s + 1 < nsegs && t >= segs[s].tile_first + segs[s].ntiles) ++s;
-  const BalSeg& sg = segs[s];
-  const int lt = t - sg.tile_first;
-  const int tok0 = sg.tok_begin + lt * T::kTile;
-  const int n = min(T::kTile, sg.ntok - lt * T::kTile);
-  const int st = t % T::kStages;
-  const uint32_t bytes = (uint32_t)n * T::kRowBytes;
-  uint8_t* stage = smem + st * T::kStageBytes;
-  mbar_arrive_expect_tx(&full[st], 2u * bytes);
-  const long long off = (long long)sg.seq * p.kv_sb + (long long)sg.kvh * p.kv_sh + (long long)tok0 * D;
-  bulk_g2s(stage, p.k + off, bytes, &full[st], pol);
-  bulk_g2s(stage + T::kHalfStage, p.v + off, bytes, &full[st], pol);
-}
-
-template <int D, int G>
-__global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBlocks)
-    gqa_decode_balanced_kernel(const DecodeParams p) {
-  using T = Traits<D, G>;
-  using BT = BalTraits<D, G>;
-  constexpr int V = T::kVec;
-  constexpr int V2 = V / 2;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int tid = threadIdx.x;
-  const bool partial_out = p.out_acc != nullptr;
-
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::kBarOff);
-  uint64_t* empty = full + T::kStages;
-  int* refill_round = reinterpret_cast<int*>(smem + T::kCntOff);
-  int* flag = reinterpret_cast<int*>(smem + T::kFlagOff);
-  float* pbuf = reinterpret_cast<float*>(smem + T::kPbufOff);
-  float* cbuf = reinterpret_cast<float*>(smem + T::kCbufOff);
-  float* aw = reinterpret_cast<float*>(smem + BT::kMergeOff);  // [warps][G][D/2]
-  float* mw = aw + T::kWarps * G * BT::kHalfD;                   // [warps][G]
-  float* lw = mw + T::kWarps * G;                                // [warps][G]
-  BalSeg* segs = reinterpret_cast<BalSeg*>(smem + BT::kSegOff);
-  int* meta = reinterpret_cast<int*>(smem + BT::kMetaOff);
-
-  allow_dependent_launch();
-  grid_dependency_wait();  // the previous kernel's writes (q, lengths, cache, workspace) are visible from here
-
-  const int tpu = (p.max_seq_len + T::kTile - 1) / T::kTile;  // tiles per unit at full length
-  const long long total = (long long)p.batch * p.n_kv_heads * tpu;
-  const int per = p.chunk / T::kTile;                           // tiles per CTA
-  const long long g0 = (long long)blockIdx.x * per;
-  const long long g1 = min(g0 + per, total);
-  if (g0 >= g1) return;
-  const uint64_t pol = make_evict_first_policy();
-
-  if (tid == 0) {
-    int ns = 0, tf = 0;
-    for (long long u = g0 / tpu; u * tpu < g1 && ns < BT::kMaxSeg; ++u) {
-      BalSeg sg{};
-      const long long ub = u * tpu;
-      const int t0 = (int)(max(g0, ub) - ub);
-      const int t1 = (int)(min(g1, ub + tpu) - ub);
-      sg.row = (int)(u / p.n_kv_heads);
-      sg.kvh = (int)(u - (long long)sg.row * p.n_kv_heads);
-      sg.seq = sg.row / p.rows_per_seq;
-      const int len = seq_len_of(p, sg.seq, sg.row - sg.seq * p.rows_per_seq);
-      sg.tok_begin = t0 * T::kTile;
-      sg.ntok = max(0, min(t1 * T::kTile, len) - sg.tok_begin);
-      sg.tile_first = tf;
-      sg.ntiles = (sg.ntok + T::kTile - 1) / T::kTile;
-      tf += sg.ntiles;
-      const long long first_cta = ub / per;
-      sg.nseg = (int)((ub + tpu - 1) / per - first_cta + 1);
-      sg.slot = (int)(blockIdx.x - first_cta);
-      segs[ns++] = sg;
-    }
-    meta[0] = ns;
-    meta[1] = tf;
-    for (int s = 0; s < T::kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], T::kWarps);
-      refill_round[s] = 0;
-    }
-    flag[0] = 0;  // error
-    flag[1] = 0;  // last-segment broadcast
-    flag[2] = 0;  // tiles issued
-    mbar_fence_init();
-    const int first = tf < T::kStages ? tf : T::kStages;
-    for (int t = 0; t < first; ++t) issue_tile_balanced<D, G>(smem, full, t, segs, ns, p, pol);
-    flag[2] = first;
-  }
-  __syncthreads();
-  const int nsegs = meta[0];
-  const int ntiles = meta[1];
-
-  // lane roles: those of the per-split kernel
-  const int half = lane / T::kLPT;
-  const int c = lane % T::kLPT;
-  int xperm = 0;
-#pragma unroll
-  for (int s2 = 0; s2 < T::kHP; ++s2)
-    xperm |= ((c >> (T::kLogLPT - 1 - s2)) & 1) << (T::kLogIter - 1 - s2);
-  int yperm = 0;
-#pragma unroll
-  for (int s2 = T::kHP; s2 < T::kH; ++s2)
-    yperm |= ((c >> (T::kLogLPT - 1 - s2)) & 1) << (T::kLogG - 1 - (s2 - T::kLogIter));
-  const int t_slot = c >> T::kR;
-  const int my_g = t_slot % G;
-  const int my_it = t_slot / G;
-  const int my_tw = my_it * T::kTPI + half;
-  const bool dup_writer = (c & ((1 << T::kR) - 1)) == 0;
-  const bool head_writer = dup_writer && lane < (G << T::kR);
-
-  float2 qp[G][V2];
-  float2 acc[G][V2];
-  float m_run = -INFINITY, l_run = 0.f;
-  auto start_segment = [&](const BalSeg& sg) {
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-      load_bf16_pairs<V>(p.q + sg.row * p.q_sb + (long long)(sg.kvh * G + (g ^ yperm)) * p.q_sh + c * V, qp[g]);
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-      for (int j = 0; j < V2; ++j) acc[g][j] = make_float2(0.f, 0.f);
-    m_run = -INFINITY;
-    l_run = 0.f;
-  };
-  // Close a segment: merge the warps (two halves of the head vector through
-  // the merge area), write the unit's output or this segment's partial state,
-  // and let the unit's last segment merge the partials.  Every thread calls it
-  // for every segment, in order; a wait that timed out (ok == false) turns the
-  // writes off for the whole CTA but keeps the barriers aligned.
-  auto finish_segment = [&](const BalSeg& sg, bool ok) {
-#pragma unroll
-    for (int off = T::kLPT; off < 32; off <<= 1)
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int j = 0; j < V2; ++j) {
-          acc[g][j].x += __shfl_xor_sync(0xffffffffu, acc[g][j].x, off);
-          acc[g][j].y += __shfl_xor_sync(0xffffffffu, acc[g][j].y, off);
-        }
-    if (!ok) atomicOr(&flag[0], 1);
-    const bool single = sg.nseg == 1;
-#pragma unroll
-    for (int part = 0; part < 2; ++part) {
-      if (half == 0 && (c * V) / BT::kHalfD == part) {
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-          for (int j = 0; j < V2; j += 2)
-            *reinterpret_cast<float4*>(aw + (warp * G + g) * BT::kHalfD + c * V - part * BT::kHalfD + 2 * j) =
-                make_float4(acc[g][j].x, acc[g][j].y, acc[g][j + 1].x, acc[g][j + 1].y);
-      }
-      if (part == 0 && head_writer) {
-        mw[warp * G + my_g] = m_run;
-        lw[warp * G + my_g] = l_run;
-      }
-      __syncthreads();
-      if (!flag[0]) {
-        for (int idx = tid; idx < G * BT::kHalfD / 2; idx += T::kThreads) {
-          const int g = idx / (BT::kHalfD / 2);
-          const int dl = (idx % (BT::kHalfD / 2)) * 2;
-          const int d = part * BT::kHalfD + dl;
-          float M = -INFINITY;
-#pragma unroll
-          for (int w = 0; w < T::kWarps; ++w) M = fmaxf(M, mw[w * G + g]);
-          const float Mu = (M == -INFINITY) ? 0.f : M;
-          float L = 0.f, o0 = 0.f, o1 = 0.f;
-#pragma unroll
-          for (int w = 0; w < T::kWarps; ++w) {
-            const float sc = exp2f(mw[w * G + g] - Mu);
-            L = fmaf(lw[w * G + g], sc, L);
-            o0 = fmaf(aw[(w * G + g) * BT::kHalfD + dl], sc, o0);
-            o1 = fmaf(aw[(w * G + g) * BT::kHalfD + dl + 1], sc, o1);
-          }
-          const int h = sg.kvh * G + g;
-          const long long row = (long long)sg.row * p.n_q_heads + h;
-          if (single) {
-            if (partial_out) {
-              *reinterpret_cast<float2*>(p.out_acc + row * D + d) = make_float2(o0, o1);
-              if (d == 0) { p.out_ml[row * 2] = M; p.out_ml[row * 2 + 1] = L; }
-            } else {
-              const float inv = (L > 0.f) ? 1.f / L : 0.f;
-              *reinterpret_cast<uint32_t*>(p.o + sg.row * p.o_sb + h * p.o_sh + d) = pack2_bf16(o0 * inv, o1 * inv);
-            }
-          } else {
-            const long long slot = row * p.nsplit + sg.slot;
-            *reinterpret_cast<float2*>(p.part_acc + slot * D + d) = make_float2(o0, o1);
-            if (d == 0) { p.part_ml[slot * 2] = M; p.part_ml[slot * 2 + 1] = L; }
-          }
-        }
-      }
-      __syncthreads();  // the merge area is rewritten by the next half or segment
-    }
-    if (single || flag[0]) return;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      int* ctr = p.counters + sg.row * p.n_kv_heads + sg.kvh;
-      const int prev = atomicAdd(ctr, 1);
-      const int last = (prev == sg.nseg - 1);
-      if (last) *ctr = 0;  // every other segment has arrived: reset for the next launch
-      flag[1] = last;
-    }
-    __syncthreads();
-    if (flag[1]) {
-      __threadfence();
-      merge_split_partials<D>(p, sg.row, sg.kvh, G, sg.nseg, partial_out, tid, T::kThreads);
-    }
-    __syncthreads();  // flag[1] is reused by the next segment
-  };
-
-  int s = 0;
-  start_segment(segs[0]);
-  bool ok = true;
-  for (int i = 0; i < ntiles; ++i) {
-    while (i >= segs[s].tile_first + segs[s].ntiles) {  // segment s is complete (or empty)
-      finish_segment(segs[s], ok);
-      ++s;
-      start_segment(segs[s]);
-    }
-    const int st = i % T::kStages;
-    const int round = i / T::kStages;
-    // After a timed-out wait the warp stops waiting and computing, but still
-    // walks the tiles so that it meets the segment barriers with the others.
-    if (ok && !mbar_wait_bounded(&full[st], round & 1)) ok = false;
-    if (ok) {
-      const BalSeg& sg = segs[s];
-      const uint8_t* Kt = smem + st * T::kStageBytes + warp * T::kTokPerWarp * T::kRowBytes;
-      const uint8_t* Vt = Kt + T::kHalfStage;
-      const int nvalid = min(T::kTile, sg.ntok - (i - sg.tile_first) * T::kTile) - warp * T::kTokPerWarp;
-      decode_tile<D, G>(Kt, Vt, nvalid, p.scale_log2, qp, acc, m_run, l_run,
-                        pbuf + ((i & 1) * T::kWarps + warp) * (T::kTokPerWarp * G),
-                        cbuf + ((i & 1) * T::kWarps + warp) * G, half, c, xperm, my_tw, my_g, dup_writer,
-                        head_writer);
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&empty[st]);
-        const int nxt = i + T::kStages;
-        if (nxt < ntiles && mbar_test_wait(&empty[st], round & 1) &&
-            atomicCAS(&refill_round[st], round, round + 1) == round) {
-          issue_tile_balanced<D, G>(smem, full, nxt, segs, nsegs, p, pol);
-          atomicMax(&flag[2], nxt + 1);
-        }
-      }
-    }
-  }
-  while (true) {
-    finish_segment(segs[s], ok);
-    if (++s >= nsegs) break;
-    start_segment(segs[s]);
-  }
-  if (flag[0] && tid == 0) {
-    atomicOr(p.status, kDevWaitTimeout);
-    // let copies already issued land before the CTA retires
-    const int issued = flag[2];
-    for (int t = (issued > T::kStages ? issued - T::kStages : 0); t < issued; ++t)
-      (void)mbar_wait_bounded(&full[t % T::kStages], (t / T::kStages) & 1);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 
@@ -942,28 +619,6 @@ KernelInfo info_for(bool paged) {
 KernelInfo lookup(int D, int G, bool paged = false) {
 #define LARA_CASE(d, g) \
   if (D == d && G == g) return info_for<d, g>(paged);
-  LARA_CASE(128, 1) LARA_CASE(128, 2) LARA_CASE(128, 4) LARA_CASE(128, 8)
-  LARA_CASE(64, 1) LARA_CASE(64, 2) LARA_CASE(64, 4) LARA_CASE(64, 8)
-#undef LARA_CASE
-  return KernelInfo{};
-}
-
-template <int D, int G>
-KernelInfo balanced_info_for() {
-  if constexpr (BalTraits<D, G>::kFits) {
-    using T = Traits<D, G>;
-    return KernelInfo{reinterpret_cast<const void*>(&gqa_decode_balanced_kernel<D, G>), T::kThreads,
-                      BalTraits<D, G>::kSmemBytes, T::kTile};
-  } else {
-    return KernelInfo{};
-  }
-}
-
-// The balanced-schedule kernel of a geometry (fn == nullptr when its shared
-// memory does not fit two CTAs per SM).
-KernelInfo lookup_balanced(int D, int G) {
-#define LARA_CASE(d, g) \
-  if (D == d && G == g) return balanced_info_for<d, g>();
   LARA_CASE(128, 1) LARA_CASE(128, 2) LARA_CASE(128, 4) LARA_CASE(128, 8)
   LARA_CASE(64, 1) LARA_CASE(64, 2) LARA_CASE(64, 4) LARA_CASE(64, 8)
 #undef LARA_CASE
@@ -1024,20 +679,6 @@ int decode_chunk_granule(int head_dim, int group) {
   return decode_tc_selected(head_dim, group) ? 128 : 0;
 }
 
-int balanced_tile_tokens(int head_dim, int group) {
-  const KernelInfo k = lookup_balanced(head_dim, group);
-  return k.fn ? k.tile : 0;
-}
-
-int balanced_partial_slots(int max_seq_len, int chunk_tokens, int head_dim, int group) {
-  const int tile = balanced_tile_tokens(head_dim, group);
-  if (tile <= 0 || chunk_tokens <= 0) return 0;
-  const int tpu = (max_seq_len + tile - 1) / tile;
-  const int per = chunk_tokens / tile;
-  if (per < 1 || (long long)per > (long long)(kBalMaxSeg - 1) * tpu) return 0;  // a CTA's segments must fit its table
-  return (tpu + per - 1) / per + 1;
-}
-
 WorkspaceLayout decode_workspace_layout(int batch, int n_q_heads, int n_kv_heads, int head_dim, int nsplit) {
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   WorkspaceLayout w;
@@ -1051,7 +692,7 @@ WorkspaceLayout decode_workspace_layout(int batch, int n_q_heads, int n_kv_heads
 }
 
 void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max_tokens, const int32_t* lens_host,
-                 int* nsplit_out, int* chunk_out, bool allow_balanced) {
+                 int* nsplit_out, int* chunk_out) {
   const int group = n_kv_heads > 0 ? n_q_heads / n_kv_heads : 1;
   if (decode_tc_selected(head_dim, group)) {
     decode_tc_plan(batch, n_kv_heads, max_tokens, lens_host, nsplit_out, chunk_out);
@@ -1118,35 +759,10 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
   }
   *nsplit_out = best_s;
   *chunk_out = best_chunk;
-  // Balanced schedule (uniform lengths): the units' tiles cut into equal runs,
-  // one per CTA slot, so every SM streams the same bytes.  Taken when the
-  // per-split plan's busiest SM carries clearly more than the average, which
-  // happens when the units are too few to fill the SM slots evenly.
-  const KernelInfo kb = lookup_balanced(head_dim, group);
-  if (allow_balanced && uniform && kb.fn) {
-    const long long sms = device_sm_count();
-    const int len0 = lens_host ? (lens_host[0] < 1 ? 1 : lens_host[0]) : L;
-    const long long units = (long long)batch * n_kv_heads;
-    const long long tpu = max_tiles;
-    const int cps_b = occupancy(kb);
-    const long long slots = sms * cps_b;
-    const long long per = (units * tpu + slots - 1) / slots;                   // tiles per CTA
-    const long long max_seg = (tpu + per - 1) / per + 1;                       // partial slots per unit
-    // per SM: its CTAs' tiles plus about one tile of prologue each, and one
-    // more when a CTA closes a segment before its end
-    const double bal = (double)cps_b * (per * tile + ovh) + (per < tpu ? ovh : 0);
-    // runs of at least tpu / (kBalMaxSeg - 2) tiles keep a unit's partials few;
-    // runs of at most (kBalMaxSeg - 1) units keep a CTA's segments within its table
-    if (len0 == L && per * (kBalMaxSeg - 2) >= tpu && per <= (kBalMaxSeg - 1) * tpu && max_seg <= 65535 &&
-        bal < 0.96 * best) {
-      *nsplit_out = (int)max_seg;
-      *chunk_out = -(int)(per * tile);
-    }
-  }
 }
 
 int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long units) {
-  if (nsplit != 2 || chunk <= 0 || decode_tc_selected(head_dim, group)) return 0;
+  if (nsplit != 2 || decode_tc_selected(head_dim, group)) return 0;
   if (units < device_sm_count()) return 0;
   const int tile = decode_tile_tokens(head_dim, group);
   if (tile <= 0) return 0;
@@ -1155,45 +771,8 @@ int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long
   return c0 > chunk ? c0 : 0;  // c0 + chunk >= 2 * chunk covers what the plan covered
 }
 
-cudaError_t decode_launch(const DecodeParams& p_in, cudaStream_t stream) {
-  const int group = p_in.n_q_heads / p_in.n_kv_heads;
-  DecodeParams p = p_in;
-  if (p.chunk < 0) {
-    // balanced plan: |chunk| tokens per CTA over the units laid end to end
-    const KernelInfo kb = lookup_balanced(p.head_dim, group);
-    const int chunk = -p.chunk;
-    if (kb.fn && p.block_table == nullptr && !decode_tc_selected(p.head_dim, group)) {
-      const int slots = balanced_partial_slots(p.max_seq_len, chunk, p.head_dim, group);
-      if (chunk % kb.tile != 0 || slots == 0 || p.nsplit < slots) return cudaErrorInvalidValue;
-      const long long tpu = (p.max_seq_len + kb.tile - 1) / kb.tile;
-      const long long per = chunk / kb.tile;
-      const long long ctas = ((long long)p.batch * p.n_kv_heads * tpu + per - 1) / per;
-      if (ctas > 0x7fffffffll) return cudaErrorInvalidValue;
-      {
-        static std::mutex mu;
-        static std::set<std::pair<const void*, int>> done;
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
-        if (e != cudaSuccess) return e;
-        std::lock_guard<std::mutex> lock(mu);
-        if (!done.count({kb.fn, dev})) {
-          e = cudaFuncSetAttribute(kb.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kb.smem);
-          if (e != cudaSuccess) return e;
-          done.insert({kb.fn, dev});
-        }
-      }
-      p.chunk = chunk;
-      p.chunk0 = 0;
-      void* args[] = {&p};
-      return launch_with_pdl(kb.fn, dim3((unsigned)ctas), dim3(kb.threads), args, kb.smem, stream);
-    }
-    // No balanced kernel on this path (paged cache, tensor-core kernel or a
-    // geometry without one): the same runs as equal splits of each unit.  They
-    // need fewer partial slots than the balanced plan reserved.
-    p.chunk = chunk;
-    p.chunk0 = 0;
-    p.nsplit = (p.max_seq_len + chunk - 1) / chunk;
-  }
+cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream) {
+  const int group = p.n_q_heads / p.n_kv_heads;
   if (decode_tc_selected(p.head_dim, group)) {
     const cudaError_t e = decode_tc_launch(p, stream);
     if (e != cudaErrorNotSupported) return e;

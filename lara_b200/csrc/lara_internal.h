@@ -85,19 +85,8 @@ WorkspaceLayout decode_workspace_layout(int batch, int n_q_heads, int n_kv_heads
 // current device.  `lens_host` (optional, [batch]) are the actual lengths; a
 // ragged batch is planned by token count instead of by waves.  Returns the
 // number of splits (grid.x) and the chunk in tokens; nsplit*chunk >= max_tokens.
-// With allow_balanced (the contiguous-cache decode entry points) a uniform
-// batch whose units cannot fill the SM slots evenly gets the balanced
-// schedule instead: chunk < 0, |chunk| tokens per CTA laid over the units end
-// to end, and nsplit = the partial slots a unit may need.
 void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max_tokens, const int32_t* lens_host,
-                 int* nsplit, int* chunk, bool allow_balanced = false);
-
-// Tokens per CTA of a balanced plan's runs (the granule is the kernel tile),
-// or 0 when the geometry has no balanced kernel.  A balanced plan of
-// chunk_tokens per CTA needs nsplit >= balanced_partial_slots() (0: the runs
-// span more units than a CTA tracks).
-int balanced_tile_tokens(int head_dim, int group);
-int balanced_partial_slots(int max_seq_len, int chunk_tokens, int head_dim, int group);
+                 int* nsplit, int* chunk);
 
 // Tile size (tokens per pipeline stage) of the compiled kernel for a head
 // geometry, or 0 when no kernel is compiled for it.
