@@ -103,6 +103,8 @@ def parse_args(argv=None):
     ap.add_argument("--extra-steps", type=int, default=200,
                     help="timed steps of each config 3/4/5 record (at most --steps)")
     ap.add_argument("--no-parity", action="store_true", help="skip the post-timing oracle checks")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch every timed step from the host instead of replaying a CUDA graph of them")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
@@ -328,24 +330,42 @@ class Collectives:
         return [float(x) for x in t.tolist()]
 
 
-def timed_steps(step, steps: int, stream, comm: Collectives, sampler=None) -> float:
+def timed_steps(step, steps: int, stream, comm: Collectives, sampler=None, graph: bool = False) -> float:
     """Mean ms per step of `steps` back-to-back calls step(i), by CUDA events on
-    `stream`, with a barrier and a synchronize on both sides."""
+    `stream`, with a barrier and a synchronize on both sides.
+
+    With `graph` the `steps` calls are first captured into one CUDA graph (and
+    replayed once, untimed), and the timed region is one replay of it: the
+    same kernels on the same buffers, without a host launch per kernel, as a
+    serving loop replays its decode step.  Small steps (tens of microseconds at
+    8 sequences per GPU) are otherwise paced by the host's launch rate."""
     import torch
 
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                step(i)
+        g.replay()
+        torch.cuda.synchronize(stream.device)
     comm.barrier()
     torch.cuda.synchronize(stream.device)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if sampler is not None:
         sampler.start()
     ev0.record(stream)
-    for i in range(steps):
-        step(i)
+    if g is not None:
+        g.replay()
+    else:
+        for i in range(steps):
+            step(i)
     ev1.record(stream)
     torch.cuda.synchronize(stream.device)
     if sampler is not None:
         sampler.stop()
     comm.barrier()
+    del g
     return ev0.elapsed_time(ev1) / steps
 
 
@@ -514,7 +534,9 @@ def decode_record(args, cfgnum: int, rank: int, world: int, dev, comm: Collectiv
     if ops.workspace_status(ws) != 0:
         raise RuntimeError(f"{cfg.name}: decode kernel reported a device error status during warm-up")
     sampler = ClockSampler(gpu_uuid(dev)) if main else None
-    ms = timed_steps(step, steps, stream, comm, sampler)
+    use_graph = not args.eager and not split  # the split-KV step holds an NCCL collective
+    run["launch"] = "CUDA graph of the timed steps, replayed once" if use_graph else "host launch per step"
+    ms = timed_steps(step, steps, stream, comm, sampler, graph=use_graph)
     clocks = sampler.summary() if sampler is not None else None
     if ops.workspace_status(ws) != 0:
         raise RuntimeError(f"{cfg.name}: decode kernel reported a device error status")
@@ -665,14 +687,14 @@ def _paged_step(args, cfg, q, k, v, lens, lens_np, o, dev):
             rows = src[b, :, : n * ps] if n * ps <= L else torch.nn.functional.pad(src[b], (0, 0, 0, n * ps - L))
             dst.index_copy_(0, pages, rows.reshape(cfg.n_kv_heads, n, ps, cfg.head_dim).permute(1, 0, 2, 3))
         base += n
-    stream = torch.cuda.current_stream(dev)
     scale = 1.0 / math.sqrt(cfg.head_dim)
 
     def step(i):
         _native.check(_native.lib.lara_gqa_decode_paged(
             q.data_ptr(), kp.data_ptr(), vp.data_ptr(), table.data_ptr(), lens.data_ptr(), o.data_ptr(), B,
             cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, ps, pps, total, scale, plan.num_splits,
-            plan.chunk_tokens, dec.workspace.data_ptr(), dec.workspace.numel(), stream.cuda_stream),
+            plan.chunk_tokens, dec.workspace.data_ptr(), dec.workspace.numel(),
+            torch.cuda.current_stream(dev).cuda_stream),  # the capture stream while a graph records
             "decode_paged")
     info = {"page_size": ps, "pages": total,
             "page_order": "random permutation (seed 7)" if args.paged_order == "random" else "sequential",
@@ -721,7 +743,7 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
         _native.check(lib.lara_gqa_prefill(c["q"].data_ptr(), c["k"].data_ptr(), c["v"].data_ptr(),
                                            p["lens0"].data_ptr(), c["o"].data_ptr(), p["nb"], n, p["nh"] * G, p["nh"], D,
                                            C + n, 1, scale, p["ws"].data_ptr(), p["ws"].numel(),
-                                           stream.cuda_stream), "prefill")
+                                           torch.cuda.current_stream(dev).cuda_stream), "prefill")
 
     def step(i):
         for p in parts:
@@ -736,11 +758,12 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
     if any(ops.workspace_status(p["ws"]) != 0 for p in parts):
         raise RuntimeError("prefill reported a device error status during warm-up")
     sampler = ClockSampler(gpu_uuid(dev)) if main else None
-    ms = timed_steps(step, steps, stream, comm, sampler)
+    ms = timed_steps(step, steps, stream, comm, sampler, graph=not args.eager)
     clocks = sampler.summary() if sampler is not None else None
     # kernel-only rate of the attention launches (the roofline's denominator time)
     k_steps = max(3, steps // 4)
-    k_ms = timed_steps(lambda i: [attend(p, p["copies"][i % R]) for p in parts], k_steps, stream, comm)
+    k_ms = timed_steps(lambda i: [attend(p, p["copies"][i % R]) for p in parts], k_steps, stream, comm,
+                       graph=not args.eager)
     if any(ops.workspace_status(p["ws"]) != 0 for p in parts):
         raise RuntimeError("prefill reported a device error status")
 
@@ -784,6 +807,7 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
                                f"{len(parts)} launch group(s)",
                 "step": "length reset + K/V append + attention (3 kernels per launch group: append, length "
                         "update, prefill)",
+                "launch": "host launch per step" if args.eager else "CUDA graph of the timed steps, replayed once",
                 "p_precision": "bf16 RNE (LARA_TC_SPLIT_P=0)" if os.environ.get("LARA_TC_SPLIT_P") == "0"
                 else "P_hi + P_lo", "input_copies": R,
                 "l2": f"{R} copies of the rank's inputs rotated (>= 4x L2 between re-reads)" if R > 1
@@ -910,6 +934,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     for name, rec in extras.items():
         line[name] = _public(rec)
     print(json.dumps(line), flush=True)
+    # a timed region that ran less work than it counts would read far above the
+    # copy-bandwidth / GEMM peak that the roofline divides by
+    implausible = [n for n, r in [("main", main)] + list(extras.items()) if r["roofline"]["frac"] > 1.5]
+    if implausible:
+        print(f"roofline fraction above 1.5 for: {implausible}", file=sys.stderr)
+        return 1
     bad = [n for n, r in [("main", main)] + list(extras.items()) if r.get("parity") and not r["parity"]["ok"]]
     if bad:
         print(f"parity check failed for: {bad}", file=sys.stderr)
