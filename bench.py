@@ -16,6 +16,9 @@ with queries/s = sequences / step time beside it.
   stream, barrier + synchronize on both sides, max over ranks).  Inputs are
   HBM-resident and larger than L2: a rank whose cache is smaller than 4x L2
   rotates over copies of it, so consecutive steps never read the same bytes.
+* launch: on one process the K timed steps are captured into one CUDA graph
+  and replayed (``--eager``: a host launch per step); runs of several ranks
+  launch every step from the host.
 * ``e2e``: the same metric through the public API with host buffers:
   ``AttentionAccelerator.run_query`` with pinned host q/o (H2D of q, decode,
   D2H of o, synchronous), wall-clock over the steps, max over ranks.
@@ -104,7 +107,8 @@ def parse_args(argv=None):
                     help="timed steps of each config 3/4/5 record (at most --steps)")
     ap.add_argument("--no-parity", action="store_true", help="skip the post-timing oracle checks")
     ap.add_argument("--eager", action="store_true",
-                    help="launch every timed step from the host instead of replaying a CUDA graph of them")
+                    help="one process: launch every timed step from the host instead of replaying a CUDA graph of "
+                         "them (runs of several ranks always launch from the host)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
@@ -534,7 +538,9 @@ def decode_record(args, cfgnum: int, rank: int, world: int, dev, comm: Collectiv
     if ops.workspace_status(ws) != 0:
         raise RuntimeError(f"{cfg.name}: decode kernel reported a device error status during warm-up")
     sampler = ClockSampler(gpu_uuid(dev)) if main else None
-    use_graph = not args.eager and not split  # the split-KV step holds an NCCL collective
+    # graphs on one process only: the split-KV step holds an NCCL collective,
+    # and an 8-rank run that captured graphs did not finish
+    use_graph = not args.eager and world == 1
     run["launch"] = "CUDA graph of the timed steps, replayed once" if use_graph else "host launch per step"
     ms = timed_steps(step, steps, stream, comm, sampler, graph=use_graph)
     clocks = sampler.summary() if sampler is not None else None
@@ -758,12 +764,13 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
     if any(ops.workspace_status(p["ws"]) != 0 for p in parts):
         raise RuntimeError("prefill reported a device error status during warm-up")
     sampler = ClockSampler(gpu_uuid(dev)) if main else None
-    ms = timed_steps(step, steps, stream, comm, sampler, graph=not args.eager)
+    use_graph = not args.eager and world == 1  # as for the decode records
+    ms = timed_steps(step, steps, stream, comm, sampler, graph=use_graph)
     clocks = sampler.summary() if sampler is not None else None
     # kernel-only rate of the attention launches (the roofline's denominator time)
     k_steps = max(3, steps // 4)
     k_ms = timed_steps(lambda i: [attend(p, p["copies"][i % R]) for p in parts], k_steps, stream, comm,
-                       graph=not args.eager)
+                       graph=use_graph)
     if any(ops.workspace_status(p["ws"]) != 0 for p in parts):
         raise RuntimeError("prefill reported a device error status")
 
@@ -807,7 +814,7 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
                                f"{len(parts)} launch group(s)",
                 "step": "length reset + K/V append + attention (3 kernels per launch group: append, length "
                         "update, prefill)",
-                "launch": "host launch per step" if args.eager else "CUDA graph of the timed steps, replayed once",
+                "launch": "CUDA graph of the timed steps, replayed once" if use_graph else "host launch per step",
                 "p_precision": "bf16 RNE (LARA_TC_SPLIT_P=0)" if os.environ.get("LARA_TC_SPLIT_P") == "0"
                 else "P_hi + P_lo", "input_copies": R,
                 "l2": f"{R} copies of the rank's inputs rotated (>= 4x L2 between re-reads)" if R > 1
