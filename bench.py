@@ -539,7 +539,7 @@ def decode_record(args, cfgnum: int, rank: int, world: int, dev, comm: Collectiv
         raise RuntimeError(f"{cfg.name}: decode kernel reported a device error status during warm-up")
     sampler = ClockSampler(gpu_uuid(dev)) if main else None
     # graphs on one process only: the split-KV step holds an NCCL collective,
-    # and an 8-rank run that captured graphs did not finish
+    # and capture beside a live NCCL process group is unmeasured here
     use_graph = not args.eager and world == 1
     run["launch"] = "CUDA graph of the timed steps, replayed once" if use_graph else "host launch per step"
     ms = timed_steps(step, steps, stream, comm, sampler, graph=use_graph)
