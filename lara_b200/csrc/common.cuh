@@ -119,6 +119,15 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
       : "memory");
 }
 
+// 2^x by the special-function unit alone: ex2.approx.ftz.f32 (relative error
+// about 2^-22; a result below 2^-126 flushes to +0, and -inf gives +0).  A
+// probability that small is below the last bit of any output it could enter.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ---- bf16 helpers --------------------------------------------------------------
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }

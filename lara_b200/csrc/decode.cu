@@ -423,13 +423,11 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
       tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
     const float m_new = fmaxf(m_run, tmax);
     const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-    const float corr = exp2f(m_run - m_use);
-    const float pr = exp2f(s - m_use);
-    float tsum = pr;
-#pragma unroll
-    for (int off = 1 << (T::kR + T::kLogG); off < 32; off <<= 1)
-      tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
-    l_run = l_run * corr + tsum;
+    const float corr = ex2_ftz(m_run - m_use);
+    const float pr = ex2_ftz(s - m_use);
+    // this lane's share of the head's running sum (the head's lanes share
+    // m_run, so their shares add up to l after the loop)
+    l_run = fmaf(l_run, corr, pr);
     // The accumulator needs rescaling only if some head's running max moved.
     const bool moved = __any_sync(0xffffffffu, m_new != m_run);
     m_run = m_new;
@@ -505,6 +503,10 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     }
   }
 
+  // The head's running sum: add the shares of its lanes (duplicate lanes of
+  // a score hold equal shares and are not added twice).
+#pragma unroll
+  for (int off = 1 << (T::kR + T::kLogG); off < 32; off <<= 1) l_run += __shfl_xor_sync(0xffffffffu, l_run, off);
   // Token rows of one pass were split across lane groups: add them up.
 #pragma unroll
   for (int off = T::kLPT; off < 32; off <<= 1)

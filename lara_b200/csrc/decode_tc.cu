@@ -18,7 +18,7 @@
 // significant bits) for a second PV pass, so the result keeps the accuracy
 // of an fp32 P.
 //
-// One CTA per SM, 6 warps:
+// One CTA per SM, 10 warps:
 //   warp 4 (TMA)   takes work items (query row, kv head, split) from a ticket
 //                  counter in the workspace and streams each item's Q (once)
 //                  and K/V tiles back to back through a 3-stage ring of
@@ -32,11 +32,17 @@
 //                  length mask, per-head tile max by redux.sync and a 4-warp
 //                  exchange, exp2, P_hi/P_lo into shared memory), and head
 //                  dim t of the output (O^T of each tile added into registers
-//                  with the online-softmax correction).  At an item's end the
-//                  row sums are reduced and the item's output or split
-//                  partial is written; the last split to finish merges.
+//                  with the online-softmax correction).  At an item's end
+//                  they hand its O^T (TMEM), row maxima and per-warp row
+//                  sums to the epilogue warps and go on with the next item.
+//   warps 6-9      epilogue, TMEM lane t = head dim t: normalise and write
+//                  the item's output, or write its split partial and, as the
+//                  last split of the row to finish, merge the partials.  The
+//                  global-memory round trips of an item's end (fence,
+//                  arrival counter, merge) are off the streaming path.
 //
-// TMEM: S^T in columns [0, 32) (two buffers of 16), O^T in [32, 64).
+// TMEM: S^T in columns [0, 32) (two buffers of 16), O^T in [32, 64), the
+// epilogue hand-off in [64, 96) (two buffers of 16).
 // Every wait is bounded by %globaltimer (the 128 softmax threads also meet on
 // an mbarrier rather than bar.sync); on a timeout the CTA flags the status
 // word, drains its own tensor-core work and copies, frees TMEM and returns.
@@ -79,12 +85,14 @@ constexpr int kXOff = kPOff + 4 * kOpBytes;         // exchange: tile max [2][4]
 constexpr int kMetaOff = kXOff + 1024;
 constexpr int kBarOff = kMetaOff + 256;
 constexpr int kPageCache = 512;                     // block-table entries of an item kept in shared memory
-constexpr int kPageOff = kBarOff + 256;
+constexpr int kHandOff = kBarOff + 256;             // epilogue hand-off descriptors (two)
+constexpr int kPageOff = kHandOff + 1024;
 constexpr int kSmemAlloc = kPageOff + kPageCache * 4 + 1024;  // + slack for 1024-byte alignment
-constexpr uint32_t kTmemCols = 64;
+constexpr uint32_t kTmemCols = 128;
+constexpr uint32_t kHandCol = 64;                   // TMEM columns of the hand-off buffers
 constexpr int kTmaWarp = 4;
 constexpr int kMmaWarp = 5;
-constexpr int kThreads = 6 * 32;
+constexpr int kThreads = 10 * 32;                   // warps 6-9 (epilogue): TMEM lane quarters 2, 3, 0, 1
 constexpr unsigned kFull = 0xffffffffu;
 
 enum : int { kEntryTile = 0, kEntryZero = 1, kEntryEnd = 2 };
@@ -117,12 +125,30 @@ struct Bars {
   uint64_t o_full[2];
   uint64_t sync;   // the 128 softmax threads
   uint64_t drain;
+  uint64_t epi_full[2];  // hand-off written (128 softmax arrivals)
+  uint64_t epi_free[2];  // hand-off read (128 epilogue arrivals)
+  uint64_t esync;        // the 128 epilogue threads
   uint32_t tmem_base;
   int abort;
   int issued;      // ring entries pushed
   int q_issued;    // Q loads issued
+  int last_split;  // epilogue: this CTA merges the row's splits
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
+
+// An item's result handed from the softmax warps to the epilogue warps (its
+// O^T columns travel in TMEM).
+struct Hand {
+  int kind;      // kEntryTile (an item's result) or kEntryEnd
+  int row;
+  int kvh;
+  int split;
+  int nsplit_b;
+  int pad[3];
+  float m[16];     // running max per head (log2 domain)
+  float l[4][16];  // row-sum share of each softmax warp
+};
+static_assert(2 * sizeof(Hand) <= 1024, "hand-off block");
 
 struct TcDecodeArgs {
   unsigned n_items;  // nsplit * batch * n_kv_heads
@@ -256,6 +282,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&bars->sync, 128);
     mbar_init(&bars->drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->epi_full[i], 128);
+      mbar_init(&bars->epi_free[i], 128);
+    }
+    mbar_init(&bars->esync, 128);
     bars->abort = 0;
     bars->issued = 0;
     bars->q_issued = 0;
@@ -582,13 +613,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&bars->drain);
       (void)mbar_wait_bounded(&bars->drain, 0);
     }
-  } else {
+  } else if (warp < 4) {
     // ------------------------------------------------------------- softmax
     const int t = threadIdx.x;  // token of a tile (S^T lane) and head dim (O^T lane)
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
     float* xmax = reinterpret_cast<float*>(smem + kXOff);  // [2][4][16]
-    float* lsum = xmax + 2 * 4 * 16;                        // [4][16]
-    volatile int* bcast = reinterpret_cast<volatile int*>(lsum + 4 * 16);
     const bool partial_out = p.out_acc != nullptr;
     uint32_t sync_phase = 0;
     int xpar = 0;
@@ -618,58 +647,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
 
-    auto epilogue = [&](const Meta& m) -> bool {
-      float L[G];
+    // An item's end: its O^T goes to the hand-off buffer in TMEM, the row
+    // maxima and each warp's row-sum share to shared memory, and the
+    // epilogue warps take it from there.
+    Hand* hand = reinterpret_cast<Hand*>(smem + kHandOff);
+    int hn = 0;  // items handed off
+    auto handoff = [&](const Meta& m, int kind) -> bool {
+      const int hs = hn & 1;
+      if (hn >= 2 && !__all_sync(kFull, wait_or_abort(&bars->epi_free[hs], ((hn - 2) >> 1) & 1, abort)))
+        return false;
+      tc_fence_after();
+      Hand& h = hand[hs];
+      if (kind == kEntryTile) {
+        uint32_t w[16];
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float v = l_part[g];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off);
-        L[g] = v;
-      }
-      if (lane == 0) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) lsum[warp * 16 + g] = L[g];
-      }
-      if (!group_sync(&bars->sync, sync_phase, abort)) return false;
-#pragma unroll
-      for (int g = 0; g < G; ++g) L[g] = (lsum[g] + lsum[16 + g]) + (lsum[32 + g] + lsum[48 + g]);
-      const int b = m.row, kvh = m.kvh;
-      if (m.nsplit_b == 1) {
+        for (int g = 0; g < 16; ++g) w[g] = g < G ? __float_as_uint(o_acc[g]) : 0u;
+        tmem_st16(lane_base + kHandCol + hs * 16, w);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          const int h = kvh * G + g;
-          const long long row = (long long)b * p.n_q_heads + h;
-          if (partial_out) {
-            p.out_acc[row * kD + t] = o_acc[g];
-            if (t == 0) { p.out_ml[row * 2] = m_run[g]; p.out_ml[row * 2 + 1] = L[g]; }
-          } else {
-            const float inv = (L[g] > 0.f) ? 1.f / L[g] : 0.f;
-            p.o[b * p.o_sb + h * p.o_sh + t] = (uint16_t)f32_to_bf16_rne_bits(o_acc[g] * inv);
-          }
-        }
-        return true;
-      }
+          float v = l_part[g];
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const long long slot = ((long long)b * p.n_q_heads + kvh * G + g) * p.nsplit + m.split;
-        p.part_acc[slot * kD + t] = o_acc[g];
-        if (t == 0) { p.part_ml[slot * 2] = m_run[g]; p.part_ml[slot * 2 + 1] = L[g]; }
+          for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(kFull, v, off);
+          if (lane == 0) h.l[warp][g] = v;
+        }
+        if (t == 0) {
+          h.row = m.row;
+          h.kvh = m.kvh;
+          h.split = m.split;
+          h.nsplit_b = m.nsplit_b;
+#pragma unroll
+          for (int g = 0; g < G; ++g) h.m[g] = m_run[g];
+        }
+        tmem_wait_st();
       }
-      __threadfence();
-      if (!group_sync(&bars->sync, sync_phase, abort)) return false;
-      if (t == 0) {
-        int* ctr = p.counters + b * p.n_kv_heads + kvh;
-        const int prev = atomicAdd(ctr, 1);
-        const int last = (prev == m.nsplit_b - 1);
-        if (last) *ctr = 0;  // every other split has arrived: reset for the next launch
-        *bcast = last;
-      }
-      if (!group_sync(&bars->sync, sync_phase, abort)) return false;
-      if (*bcast) {
-        __threadfence();
-        merge_splits_tc<G>(p, b, kvh, m.nsplit_b, partial_out, warp, lane);
-      }
+      if (t == 0) h.kind = kind;
+      tc_fence_before();
+      mbar_arrive(&bars->epi_full[hs]);
+      ++hn;
       return true;
     };
 
@@ -704,10 +718,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int g = 0; g < G; ++g) {
         const float tmax = fmaxf(fmaxf(xb[g], xb[16 + g]), fmaxf(xb[32 + g], xb[48 + g]));
         const float m_new = fmaxf(m_run[g], tmax);
-        alpha_cur[g] = (m_new == m_run[g]) ? 1.f : exp2f(m_run[g] - m_new);
+        alpha_cur[g] = (m_new == m_run[g]) ? 1.f : ex2_ftz(m_run[g] - m_new);
         m_run[g] = m_new;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        const float pr = exp2f(sv[g] - m_use);
+        const float pr = ex2_ftz(sv[g] - m_use);
         l_part[g] = fmaf(l_part[g], alpha_cur[g], pr);
         // pr - bf16(pr) is exact in fp32; its bf16 rounding carries the next 8 bits
         const __nv_bfloat16 hb = __float2bfloat16_rn(pr);
@@ -724,6 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     bool pending = false;  // O^T of the previous entry (a tile) not yet added
+    bool ended = false;
     Meta item{};
     for (int n = 0;; ++n) {
       const int st = n % kStages;
@@ -732,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool cont = m.kind == kEntryTile && !(m.flags & 1);
       if (pending && !cont) {
         // the previous item ended with tile n-1: finish it first
-        if (!accumulate(n - 1) || !epilogue(item)) break;
+        if (!accumulate(n - 1) || !handoff(item, kEntryTile)) break;
         pending = false;
       }
       if (m.kind == kEntryTile && (m.flags & 1)) {
@@ -770,7 +785,73 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        break;  // end of work
+        ended = true;  // end of work
+        break;
+      }
+    }
+    if (ended) (void)handoff(item, kEntryEnd);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Thread te owns head dim te (its TMEM lane) of every handed-off item.
+    const int te = (warp & 3) * 32 + lane;
+    const uint32_t e_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const Hand* hand = reinterpret_cast<const Hand*>(smem + kHandOff);
+    const bool partial_out = p.out_acc != nullptr;
+    uint32_t esync_phase = 0;
+    for (int hn = 0;; ++hn) {
+      const int hs = hn & 1;
+      if (!__all_sync(kFull, wait_or_abort(&bars->epi_full[hs], (hn >> 1) & 1, abort))) break;
+      tc_fence_after();
+      const Hand& h = hand[hs];
+      if (h.kind != kEntryTile) break;
+      float ov[16];
+      tmem_ld16(e_base + kHandCol + hs * 16, ov);
+      const int b = h.row, kvh = h.kvh, split = h.split, nsplit_b = h.nsplit_b;
+      float M[G], L[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        M[g] = h.m[g];
+        L[g] = (h.l[0][g] + h.l[1][g]) + (h.l[2][g] + h.l[3][g]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars->epi_free[hs]);  // the buffer may take the next item's result
+      if (nsplit_b == 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const int hq = kvh * G + g;
+          const long long row = (long long)b * p.n_q_heads + hq;
+          if (partial_out) {
+            p.out_acc[row * kD + te] = ov[g];
+            if (te == 0) { p.out_ml[row * 2] = M[g]; p.out_ml[row * 2 + 1] = L[g]; }
+          } else {
+            const float inv = (L[g] > 0.f) ? 1.f / L[g] : 0.f;
+            p.o[b * p.o_sb + hq * p.o_sh + te] = (uint16_t)f32_to_bf16_rne_bits(ov[g] * inv);
+          }
+        }
+        continue;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const long long slot = ((long long)b * p.n_q_heads + kvh * G + g) * p.nsplit + split;
+        p.part_acc[slot * kD + te] = ov[g];
+        if (te == 0) { p.part_ml[slot * 2] = M[g]; p.part_ml[slot * 2 + 1] = L[g]; }
+      }
+      __threadfence();
+      if (!group_sync(&bars->esync, esync_phase, abort)) break;
+      if (te == 0) {
+        int* ctr = p.counters + b * p.n_kv_heads + kvh;
+        const int prev = atomicAdd(ctr, 1);
+        const int last = (prev == nsplit_b - 1);
+        if (last) *ctr = 0;  // every other split has arrived: reset for the next launch
+        bars->last_split = last;
+      }
+      if (!group_sync(&bars->esync, esync_phase, abort)) break;
+      // (thread 0 writes the next item's flag only after all 128 threads have
+      // met again, so each reads this one first)
+      if (*reinterpret_cast<volatile int*>(&bars->last_split)) {
+        __threadfence();
+        merge_splits_tc<G>(p, b, kvh, nsplit_b, partial_out, warp & 3, lane);
       }
     }
   }
@@ -818,8 +899,11 @@ DecodePath path_override() {
   return DecodePath::kAuto;
 }
 
-// Groups at or above this size run on the tensor cores by default.  Below it
-// the CUDA-core kernel streams K/V at the HBM rate already.
+// Groups at or above this size run on the tensor cores by default: below 8
+// query heads per KV head the CUDA-core kernel streams at the HBM rate with P
+// kept in fp32 (config 2 under sustained load on B200: 0.955 of the copy
+// peak at 1762 MHz; this kernel, forced with LARA_DECODE_PATH=tc, 0.981 at
+// 1965 MHz, with the split-P representation error of its P.V).
 constexpr int kAutoMinGroup = 8;
 
 template <bool kPaged>

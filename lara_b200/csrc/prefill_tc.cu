@@ -322,11 +322,11 @@ __global__ void __launch_bounds__(PPLayout<kRowThreads>::kThreads, 1)
           const float m_tile = mx * a.scale_log2;  // scale > 0 keeps the order
           const bool move = m_tile > m_ref_t + kRescaleThreshold || (m_ref_t == -INFINITY && m_tile != -INFINITY);
           const float m_new = move ? m_tile : m_ref_t;
-          const float corr = move ? exp2f(m_ref_t - m_new) : 1.f;
+          const float corr = move ? ex2_ftz(m_ref_t - m_new) : 1.f;
           const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
           // packed fp32 pairs: scale-and-shift, sum and the split residual each
           // take one FFMA2 / FADD2 per two scores; exp2 is the MUFU instruction
-          // (ex2.approx, relative error ~2^-22, far below the 2^-16 of split P)
+          // (ex2.approx.ftz, relative error ~2^-22, far below the 2^-16 of split P)
           float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
           const float2 sc2 = make_float2(a.scale_log2, a.scale_log2);
           const float2 nm2 = make_float2(-m_use, -m_use);
@@ -338,8 +338,8 @@ __global__ void __launch_bounds__(PPLayout<kRowThreads>::kThreads, 1)
             for (int i = 0; i < 32; i += 2) {
               const float2 x = __ffma2_rn(make_float2(sv[c + i], sv[c + i + 1]), sc2, nm2);
               float2 pp;
-              asm("ex2.approx.f32 %0, %1;" : "=f"(pp.x) : "f"(x.x));
-              asm("ex2.approx.f32 %0, %1;" : "=f"(pp.y) : "f"(x.y));
+              pp.x = ex2_ftz(x.x);
+              pp.y = ex2_ftz(x.y);
               sum2[(i >> 1) & 1] = __fadd2_rn(sum2[(i >> 1) & 1], pp);
               const __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
               const uint32_t hw = *reinterpret_cast<const uint32_t*>(&pb);
@@ -458,11 +458,11 @@ __global__ void __launch_bounds__(PPLayout<kRowThreads>::kThreads, 1)
         const float m_tile = mx * a.scale_log2;
         const bool move = m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY);
         const float m_new = move ? m_tile : m_ref;
-        const float corr = move ? exp2f(m_ref - m_new) : 1.f;
+        const float corr = move ? ex2_ftz(m_ref - m_new) : 1.f;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
         // packed fp32 pairs: scale-and-shift, sum and the split residual each take
         // one FFMA2 / FADD2 per two scores; exp2 is the MUFU instruction
-        // (ex2.approx, relative error ~2^-22, far below the 2^-16 of split P)
+        // (ex2.approx.ftz, relative error ~2^-22, far below the 2^-16 of split P)
         float2 sum4[4];
   #pragma unroll
         for (int i = 0; i < 4; ++i) sum4[i] = make_float2(0.f, 0.f);
@@ -476,8 +476,8 @@ __global__ void __launch_bounds__(PPLayout<kRowThreads>::kThreads, 1)
           for (int i = 0; i < 32; i += 2) {
             const float2 x = __ffma2_rn(make_float2(sv[c + i], sv[c + i + 1]), sc2, nm2);
             float2 pp;
-            asm("ex2.approx.f32 %0, %1;" : "=f"(pp.x) : "f"(x.x));
-            asm("ex2.approx.f32 %0, %1;" : "=f"(pp.y) : "f"(x.y));
+            pp.x = ex2_ftz(x.x);
+            pp.y = ex2_ftz(x.y);
             sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], pp);
             const __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
             const uint32_t hw = *reinterpret_cast<const uint32_t*>(&pb);

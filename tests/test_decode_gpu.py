@@ -84,6 +84,20 @@ def test_decode_forced_splits(dev, splits):
     assert_bf16_parity(o, gold, g64, what=f"splits={splits}", tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
+@pytest.mark.parametrize("splits", [(0, 0), (4, 1024), (7, 640), (64, 64)])
+def test_decode_cuda_core_group4(dev, monkeypatch, splits):
+    """The CUDA-core kernel on the Llama-3-8B geometry (G = 4 runs on the
+    tensor cores by default; LARA_DECODE_PATH=simt selects this kernel)."""
+    from lara_b200 import ops
+
+    monkeypatch.setenv("LARA_DECODE_PATH", "simt")
+    B, Hq, Hkv, D, cap = 3, 32, 8, 128, 4096
+    assert ops.decode_kernel(Hq, Hkv, D) == "cuda_core"
+    lens = [4096, 2999, 65]
+    o, gold, g64, _ = _run_case(dev, B, Hq, Hkv, D, lens, cap, seed=17, std=0.5, splits=splits)
+    assert_bf16_parity(o, gold, g64, what=f"cuda-core G=4 splits={splits}", tensor_core=False)
+
+
 def test_decode_repeat_is_deterministic_and_counters_reset(dev):
     from lara_b200 import ops
 
@@ -221,7 +235,8 @@ def test_partial_plus_lse_combine_equals_full(dev):
     o = ops.lse_combine(torch.stack(mls), torch.stack(accs)).view(B, Hq, D)
     qw, kw, vw = words_of(q), words_of(k), words_of(v)
     gold = oracle.decode_attention(qw, kw, vw, np.full(B, L))
-    assert_bf16_parity(words_of(o), gold, oracle.decode_attention_fp64(qw, kw, vw, np.full(B, L)), what="combine")
+    assert_bf16_parity(words_of(o), gold, oracle.decode_attention_fp64(qw, kw, vw, np.full(B, L)), what="combine",
+                       tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
 def test_rejects_bad_geometry(dev):
@@ -255,7 +270,8 @@ def test_config2_full_size_sampled(dev):
         g64 = oracle.decode_attention_fp64(qw[b:b + 1], kw, vw, np.array([4096]), pairs=[(0, h) for h in hs])
         for h in hs:
             sl = slice(h * G, (h + 1) * G)
-            assert_bf16_parity(o[b, sl], gold[0, sl], g64[0, sl], what=f"cfg2 b={b} kvh={h}")
+            assert_bf16_parity(o[b, sl], gold[0, sl], g64[0, sl], what=f"cfg2 b={b} kvh={h}",
+                               tensor_core=decode_on_tensor_cores(cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim))
 
 
 @pytest.mark.slow
@@ -339,5 +355,8 @@ def test_config4_long_context_sampled(dev):
         qs = qw[b:b + 1, h * G:(h + 1) * G]
         gold = oracle.decode_attention(qs, kw, vw, np.array([L]))
         g64 = oracle.decode_attention_fp64(qs, kw, vw, np.array([L]))
-        assert_bf16_parity(o_full[b, h * G:(h + 1) * G], gold[0], g64[0], what=f"cfg4 full b={b} kvh={h}")
-        assert_bf16_parity(o_split[b, h * G:(h + 1) * G], gold[0], g64[0], what=f"cfg4 split b={b} kvh={h}")
+        tc = decode_on_tensor_cores(cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim)
+        assert_bf16_parity(o_full[b, h * G:(h + 1) * G], gold[0], g64[0], what=f"cfg4 full b={b} kvh={h}",
+                           tensor_core=tc)
+        assert_bf16_parity(o_split[b, h * G:(h + 1) * G], gold[0], g64[0], what=f"cfg4 split b={b} kvh={h}",
+                           tensor_core=tc)

@@ -299,7 +299,7 @@ def test_tc_plan_matches_list_schedule_model(tc):
 
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     cases = [(CONFIGS[3].lens(), 32768), (CONFIGS[3].lens(16), 32535), (np.full(64, 4096), 4096),
-             (np.array([0, 5, 3000, 129]), 3000)]
+             (np.full(8, 4096), 4096), (np.full(16, 4096), 4096), (np.array([0, 5, 3000, 129]), 3000)]
     for lens, L in cases:
         lens = np.ascontiguousarray(lens, np.int32)
         ns, ch = ctypes.c_int(0), ctypes.c_int(0)
