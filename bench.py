@@ -16,9 +16,9 @@ with queries/s = sequences / step time beside it.
   stream, barrier + synchronize on both sides, max over ranks).  Inputs are
   HBM-resident and larger than L2: a rank whose cache is smaller than 4x L2
   rotates over copies of it, so consecutive steps never read the same bytes.
-* launch: on one process the K timed steps are captured into one CUDA graph
-  and replayed (``--eager``: a host launch per step); runs of several ranks
-  launch every step from the host.
+* launch: the K timed steps are captured into one CUDA graph and replayed
+  (``--eager``: a host launch per step); the split-KV step, which holds an
+  NCCL collective, is launched from the host.
 * ``e2e``: the same metric through the public API with host buffers:
   ``AttentionAccelerator.run_query`` with pinned host q/o (H2D of q, decode,
   D2H of o, synchronous), wall-clock over the steps, max over ranks.
@@ -107,8 +107,7 @@ def parse_args(argv=None):
                     help="timed steps of each config 3/4/5 record (at most --steps)")
     ap.add_argument("--no-parity", action="store_true", help="skip the post-timing oracle checks")
     ap.add_argument("--eager", action="store_true",
-                    help="one process: launch every timed step from the host instead of replaying a CUDA graph of "
-                         "them (runs of several ranks always launch from the host)")
+                    help="launch every timed step from the host instead of replaying a CUDA graph of them")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
@@ -348,7 +347,9 @@ def timed_steps(step, steps: int, stream, comm: Collectives, sampler=None, graph
     g = None
     if graph:
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        # thread-local capture: other threads of the process (the process
+        # group's watchdog, the clock sampler) keep their CUDA calls
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
             for i in range(steps):
                 step(i)
         g.replay()
@@ -538,9 +539,7 @@ def decode_record(args, cfgnum: int, rank: int, world: int, dev, comm: Collectiv
     if ops.workspace_status(ws) != 0:
         raise RuntimeError(f"{cfg.name}: decode kernel reported a device error status during warm-up")
     sampler = ClockSampler(gpu_uuid(dev)) if main else None
-    # graphs on one process only: the split-KV step holds an NCCL collective,
-    # and capture beside a live NCCL process group is unmeasured here
-    use_graph = not args.eager and world == 1
+    use_graph = not args.eager and not split  # the split-KV step holds an NCCL collective
     run["launch"] = "CUDA graph of the timed steps, replayed once" if use_graph else "host launch per step"
     ms = timed_steps(step, steps, stream, comm, sampler, graph=use_graph)
     clocks = sampler.summary() if sampler is not None else None
@@ -764,7 +763,7 @@ def prefill_record(args, rank: int, world: int, dev, comm: Collectives, *, steps
     if any(ops.workspace_status(p["ws"]) != 0 for p in parts):
         raise RuntimeError("prefill reported a device error status during warm-up")
     sampler = ClockSampler(gpu_uuid(dev)) if main else None
-    use_graph = not args.eager and world == 1  # as for the decode records
+    use_graph = not args.eager
     ms = timed_steps(step, steps, stream, comm, sampler, graph=use_graph)
     clocks = sampler.summary() if sampler is not None else None
     # kernel-only rate of the attention launches (the roofline's denominator time)
