@@ -220,6 +220,29 @@ __device__ __forceinline__ void issue_tile_paged_warp(uint8_t* smem, uint64_t* f
   }
 }
 
+// VEC bf16 words from shared memory -> VEC/2 fp32 pairs (element 2i in .x,
+// 2i+1 in .y), the low element by a byte permute and the high one by a mask,
+// both on the integer ALU, so the FMA pipe keeps to the dot products.
+template <int VEC>
+__device__ __forceinline__ void load_bf16_pairs_alu(const uint16_t* p, float2 f[VEC / 2]) {
+  uint32_t w[VEC / 2];
+  if constexpr (VEC == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+  } else {
+    static_assert(VEC == 4, "VEC must be 4 or 8");
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    w[0] = u.x; w[1] = u.y;
+  }
+#pragma unroll
+  for (int i = 0; i < VEC / 2; ++i) {
+    uint32_t lo, hi;
+    asm("prmt.b32 %0, %1, 0, 0x1044;" : "=r"(lo) : "r"(w[i]));
+    asm("and.b32 %0, %1, 0xFFFF0000;" : "=r"(hi) : "r"(w[i]));
+    f[i] = make_float2(__uint_as_float(lo), __uint_as_float(hi));
+  }
+}
+
 // kPaged: K/V in a page pool addressed through the block table; each cache
 // layout gets its own instantiation, so a kernel holds only the copy code it runs.
 template <int D, int G, bool kPaged>
@@ -378,7 +401,7 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
     for (int it = 0; it < T::kIter; ++it) {
       const int tw = (it ^ xperm) * T::kTPI + half;
       float2 kp[V2];
-      load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Kt + tw * T::kRowBytes) + c * V, kp);
+      load_bf16_pairs_alu<V>(reinterpret_cast<const uint16_t*>(Kt + tw * T::kRowBytes) + c * V, kp);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         float2 a2 = __fmul2_rn(qp[g][0], kp[0]);
@@ -448,33 +471,39 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
         for (int j = 0; j < V2; ++j) acc[g][j] = __fmul2_rn(acc[g][j], cr2);
       }
     }
+    // Every warp row of a full tile holds a visible token: the per-row check
+    // is only needed on the item's last (partial) tile.
+    auto pv_row = [&](int tw) {
+      float2 vp[V2];
+      load_bf16_pairs_alu<V>(reinterpret_cast<const uint16_t*>(Vt + tw * T::kRowBytes) + c * V, vp);
+      float pg[G];
+      const float* prow = pb + tw * G;
+      if constexpr (G % 4 == 0) {
 #pragma unroll
-    for (int it = 0; it < T::kIter; ++it) {
-      const int tw = it * T::kTPI + half;
-      if (tw < nvalid) {
-        float2 vp[V2];
-        load_bf16_pairs<V>(reinterpret_cast<const uint16_t*>(Vt + tw * T::kRowBytes) + c * V, vp);
-        float pg[G];
-        const float* prow = pb + tw * G;
-        if constexpr (G % 4 == 0) {
-#pragma unroll
-          for (int g = 0; g < G; g += 4) {
-            const float4 f = *reinterpret_cast<const float4*>(prow + g);
-            pg[g] = f.x; pg[g + 1] = f.y; pg[g + 2] = f.z; pg[g + 3] = f.w;
-          }
-        } else if constexpr (G == 2) {
-          const float2 f = *reinterpret_cast<const float2*>(prow);
-          pg[0] = f.x; pg[1] = f.y;
-        } else {
-          pg[0] = prow[0];
+        for (int g = 0; g < G; g += 4) {
+          const float4 f = *reinterpret_cast<const float4*>(prow + g);
+          pg[g] = f.x; pg[g + 1] = f.y; pg[g + 2] = f.z; pg[g + 3] = f.w;
         }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float2 p2 = make_float2(pg[g], pg[g]);
-#pragma unroll
-          for (int j = 0; j < V2; ++j) acc[g][j] = __ffma2_rn(p2, vp[j], acc[g][j]);
-        }
+      } else if constexpr (G == 2) {
+        const float2 f = *reinterpret_cast<const float2*>(prow);
+        pg[0] = f.x; pg[1] = f.y;
+      } else {
+        pg[0] = prow[0];
       }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float2 p2 = make_float2(pg[g], pg[g]);
+#pragma unroll
+        for (int j = 0; j < V2; ++j) acc[g][j] = __ffma2_rn(p2, vp[j], acc[g][j]);
+      }
+    };
+    if (nvalid >= T::kTokPerWarp) {
+#pragma unroll
+      for (int it = 0; it < T::kIter; ++it) pv_row(it * T::kTPI + half);
+    } else {
+#pragma unroll
+      for (int it = 0; it < T::kIter; ++it)
+        if (it * T::kTPI + half < nvalid) pv_row(it * T::kTPI + half);
     }
     // Release the stage (mbarrier arrive: release semantics).  A warp that
     // then observes the release complete (test_wait: acquire) claims the
