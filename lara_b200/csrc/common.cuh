@@ -119,6 +119,13 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
       : "memory");
 }
 
+// Asks L2 to fetch `bytes` (multiple of 16, 16-byte aligned address) of global
+// memory; no completion is tracked.  L2 is the GPU's point of coherence, so a
+// prefetch never makes a later read return stale data, whenever it is issued.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");
+}
+
 // 2^x by the special-function unit alone: ex2.approx.ftz.f32 (relative error
 // about 2^-22; a result below 2^-126 flushes to +0, and -inf gives +0).  A
 // probability that small is below the last bit of any output it could enter.

@@ -264,11 +264,27 @@ __global__ void __launch_bounds__(Traits<D, G>::kThreads, Traits<D, G>::kMinBloc
   const bool partial_out = p.out_acc != nullptr;
 
   allow_dependent_launch();
-  grid_dependency_wait();  // the previous kernel's writes (q, lengths, cache, workspace) are visible from here
-  const int len = seq_len_of(p, seq, b - seq * p.rows_per_seq);
   // split 0 covers [0, c0), split s >= 1 covers [c0 + (s-1)*chunk, c0 + s*chunk)
   const int c0 = p.chunk0 > 0 ? p.chunk0 : p.chunk;
   const int tok_begin = split == 0 ? 0 : c0 + (split - 1) * p.chunk;
+  if constexpr (!kPaged) {
+    // With programmatic launch this CTA may be resident while the previous
+    // grid drains.  Warm L2 with the first ring tiles of its chunk meanwhile,
+    // bounded by the allocated rows (the length is not read before the wait):
+    // one lane per (tile, K or V).  A prefetch cannot return stale data, so it
+    // is safe even when the previous kernel writes the cache.
+    if (p.l2_prefetch && p.rows_per_seq == 1 && threadIdx.x < 2 * T::kStages) {
+      const int end = min(min(tok_begin + (split == 0 ? c0 : p.chunk), p.max_seq_len),
+                          tok_begin + T::kStages * T::kTile);
+      const int tok0 = tok_begin + (threadIdx.x >> 1) * T::kTile;
+      if (tok0 < end) {
+        const long long off = (long long)seq * p.kv_sb + (long long)kvh * p.kv_sh + (long long)tok0 * D;
+        bulk_prefetch_l2(((threadIdx.x & 1) ? p.v : p.k) + off, (uint32_t)min(T::kTile, end - tok0) * T::kRowBytes);
+      }
+    }
+  }
+  grid_dependency_wait();  // the previous kernel's writes (q, lengths, cache, workspace) are visible from here
+  const int len = seq_len_of(p, seq, b - seq * p.rows_per_seq);
   const int nsplit_b = len <= c0 ? 1 : 1 + (len - c0 + p.chunk - 1) / p.chunk;
 
   if (len == 0) {
@@ -803,9 +819,15 @@ int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long
 }
 
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream) {
+  static const bool prefetch = [] {
+    const char* e = std::getenv("LARA_L2_PREFETCH");
+    return !(e && e[0] == '0');
+  }();
+  DecodeParams lp = p;
+  lp.l2_prefetch = prefetch ? 1 : 0;
   const int group = p.n_q_heads / p.n_kv_heads;
   if (decode_tc_selected(p.head_dim, group)) {
-    const cudaError_t e = decode_tc_launch(p, stream);
+    const cudaError_t e = decode_tc_launch(lp, stream);
     if (e != cudaErrorNotSupported) return e;
   }
   const KernelInfo k = lookup(p.head_dim, group, p.block_table != nullptr);
@@ -833,7 +855,7 @@ cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream) {
   if (p.rows_per_seq < 1 || p.batch > 65535) return cudaErrorInvalidValue;
   if (p.nsplit > 65535) return cudaErrorInvalidValue;
   dim3 grid(p.n_kv_heads, p.batch, p.nsplit);
-  void* args[] = {const_cast<DecodeParams*>(&p)};
+  void* args[] = {&lp};
   return launch_with_pdl(k.fn, grid, dim3(k.threads), args, k.smem, stream);
 }
 

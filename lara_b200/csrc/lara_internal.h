@@ -73,6 +73,9 @@ struct DecodeParams {
   // t & ((1 << page_log2) - 1); kv_sb / kv_sh are unused.
   const int32_t* block_table;
   int page_log2, pages_per_seq, num_pages;
+  // Set by decode_launch: prefetch the CTA's first ring tiles into L2 before
+  // the dependency wait (contiguous decode rows only).
+  int l2_prefetch;
 };
 
 struct WorkspaceLayout {
