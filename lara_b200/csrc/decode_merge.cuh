@@ -15,6 +15,8 @@
 
 namespace lara {
 
+constexpr int kPreloadSplits = 8;  // split counts up to this merge from registers loaded in one batch
+
 template <int D>
 __device__ __forceinline__ void merge_split_partials(const DecodeParams& p, int b, int kvh, int group, int nsplit_b,
                                                      bool partial_out, int tid, int nthreads) {
@@ -25,16 +27,39 @@ __device__ __forceinline__ void merge_split_partials(const DecodeParams& p, int 
     const long long row = (long long)b * p.n_q_heads + h;
     const float* ml = p.part_ml + row * p.nsplit * 2;
     const float* pa = p.part_acc + row * p.nsplit * D;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < nsplit_b; ++s2) M = fmaxf(M, __ldcg(ml + s2 * 2));
-    const float Mu = (M == -INFINITY) ? 0.f : M;
-    float L = 0.f, o0 = 0.f, o1 = 0.f;
-    for (int s2 = 0; s2 < nsplit_b; ++s2) {
-      const float sc = exp2f(__ldcg(ml + s2 * 2) - Mu);
-      L = fmaf(__ldcg(ml + s2 * 2 + 1), sc, L);
-      const float2 a = __ldcg(reinterpret_cast<const float2*>(pa + (long long)s2 * D + d));
-      o0 = fmaf(a.x, sc, o0);
-      o1 = fmaf(a.y, sc, o1);
+    float M = -INFINITY, L = 0.f, o0 = 0.f, o1 = 0.f;
+    if (nsplit_b <= kPreloadSplits) {
+      // All partials are loaded at once, so the merge at the end of the
+      // kernel waits on one L2 round trip rather than one per dependent load.
+      float2 mlv[kPreloadSplits], av[kPreloadSplits];
+#pragma unroll
+      for (int s2 = 0; s2 < kPreloadSplits; ++s2)
+        if (s2 < nsplit_b) {
+          mlv[s2] = __ldcg(reinterpret_cast<const float2*>(ml + s2 * 2));
+          av[s2] = __ldcg(reinterpret_cast<const float2*>(pa + (long long)s2 * D + d));
+        }
+#pragma unroll
+      for (int s2 = 0; s2 < kPreloadSplits; ++s2)
+        if (s2 < nsplit_b) M = fmaxf(M, mlv[s2].x);
+      const float Mu = (M == -INFINITY) ? 0.f : M;
+#pragma unroll
+      for (int s2 = 0; s2 < kPreloadSplits; ++s2)
+        if (s2 < nsplit_b) {
+          const float sc = exp2f(mlv[s2].x - Mu);
+          L = fmaf(mlv[s2].y, sc, L);
+          o0 = fmaf(av[s2].x, sc, o0);
+          o1 = fmaf(av[s2].y, sc, o1);
+        }
+    } else {
+      for (int s2 = 0; s2 < nsplit_b; ++s2) M = fmaxf(M, __ldcg(ml + s2 * 2));
+      const float Mu = (M == -INFINITY) ? 0.f : M;
+      for (int s2 = 0; s2 < nsplit_b; ++s2) {
+        const float sc = exp2f(__ldcg(ml + s2 * 2) - Mu);
+        L = fmaf(__ldcg(ml + s2 * 2 + 1), sc, L);
+        const float2 a = __ldcg(reinterpret_cast<const float2*>(pa + (long long)s2 * D + d));
+        o0 = fmaf(a.x, sc, o0);
+        o1 = fmaf(a.y, sc, o1);
+      }
     }
     if (partial_out) {
       *reinterpret_cast<float2*>(p.out_acc + row * D + d) = make_float2(o0, o1);
