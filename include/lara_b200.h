@@ -83,7 +83,10 @@ LARA_API int lara_device_query(int device, lara_device_info* out);
 
 /* Split plan for a decode workload on the current device.  lens_host may be
  * NULL (every sequence is max_seq_len long) or point to B host int32 lengths.
- * Writes the split count (grid.x) and tokens per split. */
+ * Writes the split count and the tokens of splits 1..num_splits-1.  When
+ * num_splits * chunk_tokens < max_seq_len, split 0 takes the rest,
+ * max_seq_len - (num_splits - 1) * chunk_tokens rounded up to 128 tokens (the
+ * tensor-core decode's plans use this: long first items, short later ones). */
 LARA_API int lara_decode_plan(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_seq_len,
                      const int32_t* lens_host, int* num_splits, int* chunk_tokens);
 
@@ -115,7 +118,9 @@ LARA_API int lara_workspace_status(void* workspace, void* stream, int* device_st
  * bf16 in, exact products, fp32 accumulation and online softmax, bf16 RNE out.
  * seq_lens: device int32[B], each in [0, max_seq_len]; a sequence of length 0
  * gives a zero output.  num_splits/chunk_tokens come from lara_decode_plan
- * (num_splits * chunk_tokens >= max_seq_len); pass 0/0 to plan here.
+ * (any num_splits >= 1 and chunk_tokens a multiple of the kernel tile; splits
+ * that do not cover max_seq_len leave the rest to split 0, as documented at
+ * lara_decode_plan); pass 0/0 to plan here.
  * Replaces: AttentionAccelerator.run_attention (sw/attn_driver.py:469-550)
  * and the datapath it drives (hw/rtl/attn_top.sv:301-625) for one query token
  * per sequence over a resident cache. */

@@ -77,9 +77,7 @@ int resolve_plan(int batch, int hq, int hkv, int d, int lmax, const int32_t* len
     const int tile = lara::decode_chunk_granule(d, hq / hkv);
     if (*chunk % tile != 0)
       return fail(LARA_ERR_BAD_CFG, "chunk_tokens (%d) must be a multiple of the kernel tile (%d)", *chunk, tile);
-    if ((long long)*nsplit * *chunk < lmax)
-      return fail(LARA_ERR_BAD_CFG, "num_splits*chunk_tokens (%lld) must cover max_seq_len (%d)",
-                  (long long)*nsplit * *chunk, lmax);
+    // splits that do not cover lmax leave the rest to split 0 (decode_first_chunk)
     return LARA_OK;
   }
   lara::decode_plan(batch, hkv, hq, d, lmax, lens_host, nsplit, chunk);
@@ -118,7 +116,7 @@ int decode_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, const
   p.part_acc = reinterpret_cast<float*>(base + w.acc_off);
   p.out_ml = out_ml; p.out_acc = out_acc;
   p.block_table = block_table; p.page_log2 = page_log2; p.pages_per_seq = pages_per_seq; p.num_pages = num_pages;
-  p.chunk0 = lara::decode_first_chunk(nsplit, chunk, hq / hkv, d, (long long)batch * hkv);
+  p.chunk0 = lara::decode_first_chunk(nsplit, chunk, hq / hkv, d, (long long)batch * hkv, lmax);
   cudaError_t e = lara::decode_launch(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return LARA_OK;
@@ -176,6 +174,12 @@ int try_tensor_path(lara::PrefillTcParams tp, cudaStream_t st) {
   return cuda_fail(e, "tensor-core attention launch");
 }
 
+// Split 0's tokens for a plan from decode_plan on the dense and prefill rows:
+// the rest of max_seq_len when the splits do not cover it, else equal splits.
+int rest_first_chunk(int nsplit, int chunk, int hq, int hkv, int d, int lmax) {
+  return (long long)nsplit * chunk < lmax ? lara::decode_first_chunk(nsplit, chunk, hq / hkv, d, 0, lmax) : 0;
+}
+
 size_t dense_ws_bytes(int hq, int hkv, int d, int L, int* nsplit, int* chunk) {
   lara::decode_plan(L, hkv, hq, d, L, nullptr, nsplit, chunk);
   return lara::decode_workspace_layout(L, hq, hkv, d, *nsplit).total;
@@ -226,6 +230,7 @@ int dense_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16
   p.batch = L; p.n_q_heads = hq; p.n_kv_heads = hkv; p.head_dim = d;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.chunk = chunk; p.nsplit = nsplit;
+  p.chunk0 = rest_first_chunk(nsplit, chunk, hq, hkv, d, L);
   char* base = static_cast<char*>(ws);
   p.status = reinterpret_cast<int*>(base + w.status_off);
   p.counters = reinterpret_cast<int*>(base + w.counters_off);
@@ -282,6 +287,7 @@ int prefill_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
   p.batch = batch * n_new; p.n_q_heads = hq; p.n_kv_heads = hkv; p.head_dim = d;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.chunk = chunk; p.nsplit = nsplit;
+  p.chunk0 = rest_first_chunk(nsplit, chunk, hq, hkv, d, lmax);
   char* base = static_cast<char*>(ws);
   p.status = reinterpret_cast<int*>(base + w.status_off);
   p.counters = reinterpret_cast<int*>(base + w.counters_off);

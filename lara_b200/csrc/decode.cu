@@ -783,7 +783,7 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
       // with more CTAs per SM the neighbour hides each one's prologue.
       const double lone = (cps > 1 && per_sm == 1) ? 1.0 / 0.7 : 1.0;
       cost = (double)per_sm * (per + ovh) * lone;
-      const int c0 = decode_first_chunk(s_eff, chunk, group, head_dim, units);
+      const int c0 = decode_first_chunk(s_eff, chunk, group, head_dim, units, L);
       if (c0 > 0 && len0 > chunk) {
         // Long first chunks, launched first, cover every SM; the short second
         // chunks then fill whichever SM frees a slot, so the busiest SM holds
@@ -808,7 +808,17 @@ void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max
   *chunk_out = best_chunk;
 }
 
-int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long units) {
+int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long units, int max_seq_len) {
+  if (nsplit >= 1 && chunk > 0 && (long long)nsplit * chunk < max_seq_len) {
+    // Splits 1.. take `chunk` tokens each and split 0 the rest, rounded up to
+    // 128 tokens (a multiple of every kernel's tile, so either decode kernel
+    // can run the plan).
+    const int granule = decode_chunk_granule(head_dim, group);
+    if (granule <= 0) return 0;
+    const int g = 128 % granule == 0 ? 128 : granule;
+    const long long rest = (long long)max_seq_len - (long long)(nsplit - 1) * chunk;
+    return (int)((rest + g - 1) / g * g);
+  }
   if (nsplit != 2 || decode_tc_selected(head_dim, group)) return 0;
   if (units < device_sm_count()) return 0;
   const int tile = decode_tile_tokens(head_dim, group);

@@ -937,9 +937,14 @@ void decode_tc_plan(int batch, int n_kv_heads, int max_tokens, const int32_t* le
                     int* chunk_out) {
   // Items are dispensed in ticket order (split-major) to whichever CTA (one
   // per SM) is free, so the plan simulates that list schedule for each
-  // candidate chunk and keeps the one whose last CTA finishes first.  An
-  // item costs its tiles plus about one tile of stream time at its boundary
+  // candidate and keeps the one whose last CTA finishes first.  An item
+  // costs its tiles plus about one tile of stream time at its boundary
   // (B200 sweeps of configs 2 and 3: 1-3 us per item, one tile ~1.6 us).
+  // Candidates: chunks of 2^k tiles with equal splits, and with a longer
+  // split 0 (the plan's splits then cover less than max_tokens and split 0
+  // takes the rest, decode_first_chunk): every row's first item is dispensed
+  // before any short one, so long items start first and the short ones even
+  // out the finish times, as a longest-first list schedule does.
   constexpr double kItemOverhead = 1.0;
   constexpr long long kMaxItems = 1 << 18;  // candidates with more items are not simulated
   const int sms = device_sm_count() > 0 ? device_sm_count() : 148;
@@ -951,37 +956,60 @@ void decode_tc_plan(int batch, int n_kv_heads, int max_tokens, const int32_t* le
   double best = 1e300;
   int best_chunk = max_tiles * kTile, best_s = 1;
   std::vector<double> heap;
+  auto simulate = [&](long long c0, long long c, int ns) {
+    heap.assign((size_t)sms, 0.0);  // min-heap of CTA finish times
+    auto take = [&](double cost) {
+      std::pop_heap(heap.begin(), heap.end(), std::greater<double>());
+      heap.back() += cost;
+      std::push_heap(heap.begin(), heap.end(), std::greater<double>());
+    };
+    for (int sp = 0; sp < ns; ++sp)
+      for (int b = 0; b < batch; ++b) {
+        const long long begin = sp == 0 ? 0 : c0 + (long long)(sp - 1) * c;
+        if (len[b] == 0 && sp == 0) {
+          for (int h = 0; h < n_kv_heads; ++h) take(kItemOverhead);
+          continue;
+        }
+        if (begin >= len[b]) continue;
+        const long long ntok = std::min<long long>(sp == 0 ? c0 : c, len[b] - begin);
+        const double cost = (double)((ntok + kTile - 1) / kTile) + kItemOverhead;
+        for (int h = 0; h < n_kv_heads; ++h) take(cost);
+      }
+    return *std::max_element(heap.begin(), heap.end());
+  };
+  auto consider = [&](int c, int ns) {
+    const long long c0 = (long long)ns * c >= L ? c : ((L - (long long)(ns - 1) * c + kTile - 1) / kTile) * kTile;
+    long long items = 0;
+    for (int b = 0; b < batch; ++b) items += len[b] <= c0 ? 1 : 1 + (len[b] - c0 + c - 1) / c;
+    if (items * n_kv_heads > kMaxItems) return;
+    const double makespan = simulate(c0, c, ns);
+    if (makespan < best * (1.0 - 1e-9)) {
+      best = makespan;
+      best_chunk = c;
+      best_s = ns;
+    }
+  };
+  // equal splits: chunks of 2^k tiles
+  std::vector<int> chunks;
   for (long long chunk = kTile;; chunk *= 2) {
     if (chunk > (long long)max_tiles * kTile) chunk = (long long)max_tiles * kTile;
-    const int c = (int)chunk;
-    const int ns = (L + c - 1) / c;
-    if ((long long)ns * batch * n_kv_heads <= kMaxItems) {
-      heap.assign((size_t)sms, 0.0);  // min-heap of CTA finish times
-      auto take = [&](double cost) {
-        std::pop_heap(heap.begin(), heap.end(), std::greater<double>());
-        heap.back() += cost;
-        std::push_heap(heap.begin(), heap.end(), std::greater<double>());
-      };
-      for (int sp = 0; sp < ns; ++sp)
-        for (int b = 0; b < batch; ++b) {
-          const long long begin = (long long)sp * c;
-          if (len[b] == 0 && sp == 0) {
-            for (int h = 0; h < n_kv_heads; ++h) take(kItemOverhead);
-            continue;
-          }
-          if (begin >= len[b]) continue;
-          const long long ntok = std::min<long long>(c, len[b] - begin);
-          const double cost = (double)((ntok + kTile - 1) / kTile) + kItemOverhead;
-          for (int h = 0; h < n_kv_heads; ++h) take(cost);
-        }
-      const double makespan = *std::max_element(heap.begin(), heap.end());
-      if (makespan < best * (1.0 - 1e-9)) {
-        best = makespan;
-        best_chunk = c;
-        best_s = ns;
+    chunks.push_back((int)chunk);
+    consider((int)chunk, (L + (int)chunk - 1) / (int)chunk);
+    if (chunk >= (long long)max_tiles * kTile) break;
+  }
+  // a longer split 0, for the best equal-split chunk, a quarter and half of
+  // it, and twice it: split counts whose split 0 is about 1.5^j chunks long
+  const int best_equal = best_chunk;
+  for (const int c : chunks) {
+    if (c != best_equal && c * 2 != best_equal && c * 4 != best_equal && c != best_equal * 2) continue;
+    int last = (L + c - 1) / c;
+    for (double m = 1.5; m * c < L; m *= 1.5) {
+      const int ns = 1 + (int)((L - (long long)(m * c)) / c);
+      if (ns >= 1 && ns < last) {
+        consider(c, ns);
+        last = ns;
       }
     }
-    if (c >= max_tiles * kTile) break;
   }
   *nsplit_out = best_s;
   *chunk_out = best_chunk;

@@ -87,7 +87,8 @@ WorkspaceLayout decode_workspace_layout(int batch, int n_q_heads, int n_kv_heads
 // Chooses the split count for a (batch, kv heads, max tokens) workload on the
 // current device.  `lens_host` (optional, [batch]) are the actual lengths; a
 // ragged batch is planned by token count instead of by waves.  Returns the
-// number of splits (grid.x) and the chunk in tokens; nsplit*chunk >= max_tokens.
+// number of splits (grid.z) and the chunk in tokens; when nsplit*chunk < max_tokens
+// split 0 takes the rest (decode_first_chunk).
 void decode_plan(int batch, int n_kv_heads, int n_q_heads, int head_dim, int max_tokens, const int32_t* lens_host,
                  int* nsplit, int* chunk);
 
@@ -100,14 +101,18 @@ int decode_tile_tokens(int head_dim, int group);
 int decode_chunk_granule(int head_dim, int group);
 
 // Tokens of the first split for a (nsplit, chunk) plan over `units` (query
-// row, kv head) pairs, or 0 for equal splits.  With two splits the first
+// row, kv head) pairs, or 0 for equal splits.  A plan whose splits do not
+// cover max_seq_len (nsplit * chunk < max_seq_len) gives split 0 the rest,
+// max_seq_len - (nsplit - 1) * chunk rounded up to 128 tokens: long
+// first items, then short ones that even out the tail of the tensor-core
+// decode's list schedule.  Otherwise, with two splits the first
 // covers 7/8 of the span: all first chunks launch before any second chunk, so
 // the short second chunks fill the last wave (measured on B200: +1.2 to
 // +3.8 % GB/s on 64 x 4096, 64 x 8192 and 96 x 4096 decodes).  It applies
 // only when the first chunks alone occupy every SM: with fewer units, SMs
 // holding a long first chunk stream it alone while others finish early (8 x
 // 4096 ran at 0.26-0.35 of HBM, 16 x 4096 at 0.50-0.66).
-int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long units);
+int decode_first_chunk(int nsplit, int chunk, int group, int head_dim, long long units, int max_seq_len);
 
 cudaError_t decode_launch(const DecodeParams& p, cudaStream_t stream);
 

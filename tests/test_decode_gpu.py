@@ -75,19 +75,21 @@ def test_decode_geometries_ragged(dev, geom):
     assert_bf16_parity(o, gold, g64, what=str(geom), tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
-@pytest.mark.parametrize("splits", [(1, 4096), (4, 1024), (64, 64), (7, 640)])
+@pytest.mark.parametrize("splits", [(1, 4096), (4, 1024), (64, 64), (7, 640), (3, 1024), (5, 384)])
 def test_decode_forced_splits(dev, splits):
-    """Split-KV merge inside the kernel (last-arriving CTA) for several plans."""
+    """Split-KV merge inside the kernel (last-arriving CTA) for several plans,
+    including plans whose splits do not cover the cache (3 x 1024, 5 x 384 over
+    4096 tokens: split 0 takes the rest, 2048 and 2560 tokens)."""
     B, Hq, Hkv, D, cap = 2, 32, 8, 128, 4096
     lens = [4096, 2999]
     o, gold, g64, _ = _run_case(dev, B, Hq, Hkv, D, lens, cap, seed=7, std=0.5, splits=splits)
     assert_bf16_parity(o, gold, g64, what=f"splits={splits}", tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
-@pytest.mark.parametrize("splits", [(0, 0), (4, 1024), (7, 640), (64, 64)])
+@pytest.mark.parametrize("splits", [(0, 0), (4, 1024), (7, 640), (64, 64), (3, 1024)])
 def test_decode_cuda_core_group4(dev, monkeypatch, splits):
-    """The CUDA-core kernel on the Llama-3-8B geometry (G = 4 runs on the
-    tensor cores by default; LARA_DECODE_PATH=simt selects this kernel)."""
+    """The CUDA-core kernel on the Llama-3-8B geometry, selected explicitly with
+    LARA_DECODE_PATH=simt (the default for G = 4 as well)."""
     from lara_b200 import ops
 
     monkeypatch.setenv("LARA_DECODE_PATH", "simt")

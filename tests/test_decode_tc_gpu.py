@@ -109,9 +109,12 @@ def test_tc_geometries_ragged(tc, geom):
     assert_bf16_parity(o, gold, g64, what=f"tc {geom}", tensor_core=decode_on_tensor_cores(Hq, Hkv, 128))
 
 
-@pytest.mark.parametrize("splits", [(1, 4096), (4, 1024), (64, 64), (7, 640), (3, 1376)])
+@pytest.mark.parametrize("splits", [(1, 4096), (4, 1024), (64, 64), (7, 640), (3, 1376), (3, 1024), (5, 384),
+                                    (1, 128)])
 def test_tc_forced_splits(tc, splits):
-    """Split partials and the last-arriver merge for several plans (G = 8)."""
+    """Split partials and the last-arriver merge for several plans (G = 8),
+    including plans whose splits do not cover the cache, so split 0 takes the
+    rest (3 x 1024: 2048 tokens; 5 x 384: 2560; 1 x 128: all 4096)."""
     o, gold, g64, _ = _case(tc, 2, 64, 8, [4096, 2999], 4096, seed=7, std=0.5, splits=splits)
     assert_bf16_parity(o, gold, g64, what=f"tc splits={splits}", tensor_core=decode_on_tensor_cores(64, 8, 128))
 
@@ -258,37 +261,61 @@ def test_dense_transaction_on_decode_kernels(dev, monkeypatch, path):
                        tensor_core=decode_on_tensor_cores(Hq, Hkv, D))
 
 
-def _list_schedule_plan(lens, L, hkv, sms, overhead=1.0):
+def _list_schedule_plan(lens, L, hkv, sms, overhead=1.0, max_items=1 << 18):
     """The planner's model restated: items in ticket order (split-major) go to the
-    earliest-free CTA; an item costs its 128-token tiles plus `overhead` tiles."""
+    earliest-free CTA; an item costs its 128-token tiles plus `overhead` tiles.
+    Candidates: equal splits of 2^k tiles; then, for the best of those chunks,
+    a quarter and half of it and twice it, split counts whose split 0 (the
+    rest of max_seq_len, rounded up to 128 tokens) is about 1.5^j chunks long."""
     import heapq
 
     max_tiles = -(-L // 128)
-    best = None
-    c = 128
-    while True:
-        c = min(c, max_tiles * 128)
-        ns = -(-L // c)
+    best = [None]
+
+    def consider(c, ns):
+        c0 = c if ns * c >= L else -(-(L - (ns - 1) * c) // 128) * 128
+        items = sum(1 if n <= c0 else 1 + -(-(n - c0) // c) for n in lens)
+        if items * hkv > max_items:
+            return
         heap = [0.0] * sms
         for sp in range(ns):
             for n in lens:
-                begin = sp * c
+                begin = 0 if sp == 0 else c0 + (sp - 1) * c
                 if n == 0 and sp == 0:
                     for _ in range(hkv):
                         heapq.heapreplace(heap, heap[0] + overhead)
                     continue
                 if begin >= n:
                     continue
-                cost = -(-min(c, n - begin) // 128) + overhead
+                cost = -(-min(c0 if sp == 0 else c, n - begin) // 128) + overhead
                 for _ in range(hkv):
                     heapq.heapreplace(heap, heap[0] + cost)
         span = max(heap)
-        if best is None or span < best[0] * (1 - 1e-9):
-            best = (span, ns, c)
+        if best[0] is None or span < best[0][0] * (1 - 1e-9):
+            best[0] = (span, ns, c)
+
+    chunks = []
+    c = 128
+    while True:
+        c = min(c, max_tiles * 128)
+        chunks.append(c)
+        consider(c, -(-L // c))
         if c >= max_tiles * 128:
             break
         c *= 2
-    return best[1], best[2]
+    best_equal = best[0][2]
+    for c in chunks:
+        if best_equal not in (c, 2 * c, 4 * c) and c != 2 * best_equal:
+            continue
+        last = -(-L // c)
+        m = 1.5
+        while m * c < L:
+            ns = 1 + (L - int(m * c)) // c
+            if 1 <= ns < last:
+                consider(c, ns)
+                last = ns
+            m *= 1.5
+    return best[0][1], best[0][2]
 
 
 def test_tc_plan_matches_list_schedule_model(tc):
